@@ -1,0 +1,394 @@
+"""Benchmark of the sparse paged GQA FP8 decode path (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 1] [--kernel auto|tc|simt]
+
+Workload: BASELINE's headline shape, configs[1] (256 requests x 32q/8kv heads x
+d128, page 16, 32 pages/request, Top-K 512 = every token in random order) on
+every GPU -- one process per GPU under torchrun, requests sharded by rank
+with no data-path collective, so per-GPU work is fixed ("weak" scaling; at 8
+GPUs the job is configs[3]'s 2048 requests). A step is one decode call over
+the rank's batch with all inputs resident in HBM; L2 is flushed (a 256 MiB
+write) between timed steps, outside the timed events.
+
+Reported ``value``: achieved HBM TB/s on unique FP8 K/V bytes summed over
+ranks / max-over-ranks device time per call (the north star's figure);
+``us_per_call`` and ``ms_per_step`` give the latency. ``e2e`` is the same
+figure through the public ``qsa_decode`` call with the step's inputs (Q,
+gate, Top-K indices, block table, request map) copied from pinned host memory
+and the output copied back inside the timed region; the K/V cache stays
+resident (it is the cache). ``--impl reference`` times the reference's eager
+path (a port of sm89_torch.torch_eager) on the host CPU instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "qsa-fp8-sm89_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "µs/call + achieved HBM TB/s (vs ~8 TB/s) @256 req, TopK 512; 1/2/4/8 GPU"
+FLUSH_BYTES = 256 << 20
+FALLBACK_HBM_GBS = 6650.0
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch on the
+# bench workload, from the ncu capture summarised in profiles/ (None until
+# captured for the current kernel).
+NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): None}
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--kernel", default="auto")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def workload_name(cfg: int) -> str:
+    return {1: "configs[1]", 2: "configs[2]", 3: "configs[3]", 0: "configs[0]", 4: "configs[4]"}[cfg]
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML every few ms."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+# -------------------------------------------------------------- dist utils --
+def dist_setup(n_gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} needs {n_gpus} ranks (torchrun --nproc-per-node {n_gpus}); "
+                         f"WORLD_SIZE={world}")
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return rank, local, world
+
+
+def barrier(world, local):
+    import torch
+
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+
+
+def reduce_max(x: float, world: int, local: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(x: float, world: int, local: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------ CPU baseline --
+def cpu_eager_sample(w, rows: int, calls: int, warmup: int):
+    """Times the reference's eager path (CPU port) on the first ``rows``
+    requests of the workload, re-indexed into a compact host cache. Returns
+    (seconds per call list, unique K/V bytes per call, threads)."""
+    import torch
+
+    from oracle.eager_port import torch_eager_port
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sel = torch.arange(rows, device=w.btable.device)
+    bt = w.btable[w.t2r[sel].long()].long()
+    pages = torch.unique(bt)
+    remap = torch.full((w.k.shape[0],), -1, dtype=torch.long, device=bt.device)
+    remap[pages] = torch.arange(pages.numel(), device=bt.device)
+    host = dict(
+        q=w.q[sel].cpu(), gate=w.gate[sel].cpu(), k=w.k.view(torch.uint8)[pages].cpu().view(torch.float8_e4m3fn),
+        v=w.v.view(torch.uint8)[pages].cpu().view(torch.float8_e4m3fn), btable=remap[bt].to(torch.int32).cpu(),
+        t2r=torch.arange(rows, dtype=torch.int32), indices=w.indices[sel].cpu(),
+    )
+    args = (host["q"], host["k"], host["v"], w.k_scale, w.v_scale, host["btable"], host["t2r"], host["indices"],
+            host["gate"])
+    for _ in range(warmup):
+        torch_eager_port(*args)
+    times = []
+    for _ in range(calls):
+        t0 = time.perf_counter()
+        torch_eager_port(*args)
+        times.append(time.perf_counter() - t0)
+    idx = host["indices"]
+    n_valid = int((idx >= 0).sum())
+    unique_kv = n_valid * w.meta["hkv"] * 128 * 2
+    return times, unique_kv, threads
+
+
+def run_reference_arm(args):
+    """--impl reference: the reference's eager path on the host CPU."""
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(args.config, "cpu", seed=0)
+    # one step = one eager call on a bounded sample of the batch, sized so the
+    # whole --steps/--warmup run stays within a few minutes
+    probe, _, _ = cpu_eager_sample(w, 8, 1, 1)
+    per_row = max(probe[0] / 8, 1e-4)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    rows = int(max(4, min(w.rows, budget / per_row)))
+    times, unique_kv, threads = cpu_eager_sample(w, rows, args.steps, args.warmup)
+    med = statistics.median(times)
+    value = unique_kv / med / 1e12
+    sample = (f"{rows} of {w.rows} requests of {workload_name(args.config)} per call (unique K/V "
+              f"{unique_kv} B), {args.steps} timed calls after {args.warmup} warm-up, median")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3,
+        "us_per_call_full_batch": med / rows * w.rows * 1e6, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(args.config), "rows": rows, "topk": w.meta["topk"],
+                   "hq": w.meta["hq"], "hkv": w.meta["hkv"], "head_dim": 128, "page": w.meta["page"]},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port", "sample": sample,
+                         "min_s": min(times), "median_s": med, "max_s": max(times)},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- our arm ---
+def run_ours(args):
+    import torch
+
+    rank, local, world = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import qsa_b200
+    from qsa_b200 import capi
+    from qsa_b200.inputs import kv_bytes, make_workload
+
+    w = make_workload(args.config, dev, seed=0, shard=rank)
+    acct = kv_bytes(w)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    out = torch.empty_like(w.q)
+    kernel = args.kernel
+    launches_per_call = 1 + (1 if w.meta["topk"] > 512 else 0)
+
+    def call():
+        qsa_b200.qsa_decode(*w.args(), out=out, kernel=kernel)
+
+    # ---- device-resident timing --------------------------------------------
+    for _ in range(max(3, args.warmup)):
+        call()
+        flush.zero_()
+    stream = torch.cuda.current_stream()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world, local)
+    with ClockSampler(local) as clk:
+        region0 = torch.cuda.Event(enable_timing=True)
+        region1 = torch.cuda.Event(enable_timing=True)
+        region0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            call()
+            ends[i].record(stream)
+            flush.zero_()
+        region1.record(stream)
+        barrier(world, local)
+    kern_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    local_ms = sum(kern_ms) / len(kern_ms)
+    step_ms = reduce_max(local_ms, world, local)
+    total_unique = reduce_sum(acct["unique_kv"], world, local)
+    total_logical = reduce_sum(acct["logical_kv"], world, local)
+    value = total_unique / (step_ms * 1e-3) / 1e12
+
+    # ---- end to end through the public call with host buffers ---------------
+    host_in = {k: getattr(w, k).cpu().pin_memory() for k in ("q", "gate", "indices", "btable", "t2r")}
+    dev_in = {k: torch.empty_like(getattr(w, k)) for k in host_in}
+    host_out = torch.empty(w.q.shape, dtype=w.q.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_call():
+        for k, t in host_in.items():
+            dev_in[k].copy_(t, non_blocking=True)
+        qsa_b200.qsa_decode(dev_in["q"], w.k, w.v, w.k_scale, w.v_scale, dev_in["btable"], dev_in["t2r"],
+                            dev_in["indices"], dev_in["gate"], out=out, kernel=kernel)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_call()
+        flush.zero_()
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world, local)
+    for i in range(args.steps):
+        e_starts[i].record(stream)
+        e2e_call()
+        e_ends[i].record(stream)
+        flush.zero_()
+    barrier(world, local)
+    e2e_ms = reduce_max(sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)) / args.steps, world, local)
+    e2e_value = total_unique / (e2e_ms * 1e-3) / 1e12
+    torch.cuda.synchronize()
+    assert torch.equal(host_out, out.cpu())
+    dev_err = capi.device_error()
+
+    # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        times, ukv, threads = cpu_eager_sample(w, 32, 5, 3)
+        med = statistics.median(times)
+        cpu = {"value": ukv / med / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+               "sample": f"32 of {w.rows} requests of {workload_name(args.config)} per call through the "
+                         f"reference's eager ATen sequence on CPU (oracle/eager_port.py), median of 5 after 3 "
+                         f"warm-up; min {min(times):.3f} s, max {max(times):.3f} s per call",
+               "us_per_call_full_batch": med / 32 * w.rows * 1e6}
+
+    peak, peak_kind = peaks()
+    achieved_gbs = acct["algorithmic"] / (local_ms * 1e-3) / 1e9
+    kname = "tc" if kernel in ("auto", "tc") else kernel
+    traffic = NCU_TRAFFIC_BYTES.get((workload_name(args.config), kname))
+    clocks = clk.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "us_per_call": step_ms * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3 tensor-core MMA, f32 accumulate/softmax, bf16 out", "data": "synthetic",
+            "config": {"workload": workload_name(args.config), "rows_per_gpu": w.rows, "rows_total": w.rows * world,
+                       "hq": w.meta["hq"], "hkv": w.meta["hkv"], "head_dim": 128, "page": w.meta["page"],
+                       "pages_per_req": w.meta["ppr"], "topk": w.meta["topk"], "kernel": kernel,
+                       "l2": "flushed between timed steps (256 MiB write, outside the timed events)",
+                       "parallelism": f"request-sharded x{world}, no collective"},
+            "bytes_per_gpu": {"unique_kv": acct["unique_kv"], "logical_kv": acct["logical_kv"],
+                              "algorithmic": acct["algorithmic"]},
+            "logical_kv_tbs": total_logical / (step_ms * 1e-3) / 1e12,
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": achieved_gbs / peak, "peak_source": peak_kind,
+                         "traffic": traffic, "kernel": f"qsa_decode_{kname}_kernel"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": launches_per_call * args.steps,
+            "clocks": clocks,
+            "device_error": dev_err,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world, local)
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

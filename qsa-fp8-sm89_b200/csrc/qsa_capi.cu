@@ -1,0 +1,270 @@
+// C ABI of libqsa_b200.so (declared in include/qsa_b200.h).
+//
+// Validates arguments, turns them into qsa::DecodeParams and launches the
+// decode kernel (tensor-core kernel for group sizes 1/2/4/8/16, CUDA-core
+// kernel otherwise), plus the split combine when a Top-K row is longer than
+// one 512-entry chunk. No entry point allocates, synchronises or traps.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+
+#include "../../include/qsa_b200.h"
+#include "qsa_internal.h"
+
+namespace qsa {
+
+// Device error word (one per device that loads the library).
+__device__ int g_device_error = 0;
+
+namespace {
+
+thread_local int t_last_status = QSA_B200_OK;
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+// Is the current device an sm_100 part? Cached per device ordinal.
+int check_device() {
+  static std::atomic<uint64_t> ok_mask{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return QSA_B200_ERR_DEVICE;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (ok_mask.load(std::memory_order_acquire) & bit) return QSA_B200_OK;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return QSA_B200_ERR_DEVICE;
+  if (major != 10) return QSA_B200_ERR_DEVICE;
+  ok_mask.fetch_or(bit, std::memory_order_acq_rel);
+  return QSA_B200_OK;
+}
+
+// Device address of g_device_error on the current device (cached per device).
+int* device_error_word() {
+  static std::atomic<int*> addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  int* a = addr[dev & 63].load(std::memory_order_acquire);
+  if (!a) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
+    a = static_cast<int*>(ptr);
+    addr[dev & 63].store(a, std::memory_order_release);
+  }
+  return a;
+}
+
+int num_chunks_for(int topk) {
+  const int c = tc_chunk_tokens();
+  return topk <= c ? 1 : (topk + c - 1) / c;
+}
+
+// Validation of the index / table part of the arguments (shared by slots).
+int check_index_args(const qsa_b200_decode_args* a) {
+  if (!a) return QSA_B200_ERR_NULL_POINTER;
+  if (a->rows < 0 || a->topk < 0 || a->page_size < 1 || a->pages_per_req < 1 || a->num_reqs < 1 ||
+      a->num_pages < 1)
+    return QSA_B200_ERR_BAD_SHAPE;
+  if (a->rows == 0) return QSA_B200_OK;
+  if (!a->indices || !a->btable) return QSA_B200_ERR_NULL_POINTER;
+  if (a->indices_stride < (int64_t)a->topk + (a->count_column ? 1 : 0)) return QSA_B200_ERR_BAD_SHAPE;
+  if (a->btable_stride < a->pages_per_req) return QSA_B200_ERR_BAD_SHAPE;
+  if (!aligned4(a->indices) || !aligned4(a->btable) || (a->t2r && !aligned4(a->t2r)) ||
+      (a->counts && !aligned4(a->counts)))
+    return QSA_B200_ERR_MISALIGNED;
+  return QSA_B200_OK;
+}
+
+int check_decode_args(const qsa_b200_decode_args* a) {
+  int st = check_index_args(a);
+  if (st != QSA_B200_OK) return st;
+  if (a->num_q_heads < 1 || a->num_kv_heads < 1 || a->num_q_heads % a->num_kv_heads != 0)
+    return QSA_B200_ERR_BAD_SHAPE;
+  if (a->head_dim != 128) return QSA_B200_ERR_UNSUPPORTED;
+  const int group = a->num_q_heads / a->num_kv_heads;
+  if (group > 32) return QSA_B200_ERR_UNSUPPORTED;
+  if (a->kernel == QSA_B200_KERNEL_TC && !tc_supports_group(group)) return QSA_B200_ERR_UNSUPPORTED;
+  if (a->kernel < QSA_B200_KERNEL_AUTO || a->kernel > QSA_B200_KERNEL_SIMT) return QSA_B200_ERR_UNSUPPORTED;
+  if ((int64_t)a->rows * a->num_kv_heads > 0x7fffffffll) return QSA_B200_ERR_BAD_SHAPE;
+  if (a->rows == 0) return QSA_B200_OK;
+  if (!a->q || !a->k_cache || !a->v_cache || !a->gate || !a->out) return QSA_B200_ERR_NULL_POINTER;
+  if (!aligned16(a->q) || !aligned16(a->k_cache) || !aligned16(a->v_cache) || !aligned16(a->gate) ||
+      !aligned16(a->out))
+    return QSA_B200_ERR_MISALIGNED;
+  return QSA_B200_OK;
+}
+
+void fill_params(const qsa_b200_decode_args* a, DecodeParams* p) {
+  p->q = static_cast<const __nv_bfloat16*>(a->q);
+  p->gate = static_cast<const __nv_bfloat16*>(a->gate);
+  p->out = static_cast<__nv_bfloat16*>(a->out);
+  p->k = static_cast<const uint8_t*>(a->k_cache);
+  p->v = static_cast<const uint8_t*>(a->v_cache);
+  p->indices = a->indices;
+  p->counts = a->counts;
+  p->btable = a->btable;
+  p->t2r = a->t2r;
+  p->score_scale_log2 = a->softmax_scale * a->k_scale * 1.4426950408889634f;
+  p->v_scale = a->v_scale;
+  p->rows = a->rows;
+  p->num_q_heads = a->num_q_heads;
+  p->num_kv_heads = a->num_kv_heads;
+  p->group = a->num_kv_heads > 0 ? a->num_q_heads / a->num_kv_heads : 0;
+  p->page_size = a->page_size;
+  int shift = -1;
+  for (int s = 0; s < 31; ++s)
+    if ((1 << s) == a->page_size) shift = s;
+  p->page_shift = shift;
+  p->pages_per_req = a->pages_per_req;
+  p->num_reqs = a->num_reqs;
+  p->num_pages = a->num_pages;
+  p->topk = a->topk;
+  p->indices_stride = a->indices_stride;
+  p->count_column = a->count_column;
+  p->btable_stride = a->btable_stride;
+  p->chunk_tokens = tc_chunk_tokens();
+  p->num_chunks = num_chunks_for(a->topk);
+  p->part_o = nullptr;
+  p->part_lse = nullptr;
+  p->err = nullptr;
+}
+
+int64_t workspace_for(const DecodeParams& p) {
+  if (p.num_chunks <= 1) return 0;
+  const int64_t n = (int64_t)p.rows * p.num_q_heads * p.num_chunks;
+  const int64_t o_bytes = ((n * 128 * 4) + 255) / 256 * 256;
+  return o_bytes + (n * 4 + 255) / 256 * 256;
+}
+
+}  // namespace
+}  // namespace qsa
+
+using namespace qsa;
+
+extern "C" {
+
+int qsa_b200_abi_version(void) { return QSA_B200_ABI_VERSION; }
+
+const char* qsa_b200_status_string(int status) {
+  switch (status) {
+    case QSA_B200_OK: return "ok";
+    case QSA_B200_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case QSA_B200_ERR_BAD_SHAPE: return "invalid or inconsistent sizes";
+    case QSA_B200_ERR_UNSUPPORTED: return "unsupported shape (head_dim must be 128, group size <= 32)";
+    case QSA_B200_ERR_MISALIGNED: return "a tensor is not aligned (16 bytes for q/k/v/gate/out, 4 for int32)";
+    case QSA_B200_ERR_WORKSPACE: return "workspace missing or too small";
+    case QSA_B200_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) part";
+    case QSA_B200_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case QSA_B200_ERR_KERNEL: return "a kernel reported a device-side failure";
+    default: return "unknown status";
+  }
+}
+
+int64_t qsa_b200_workspace_bytes(const qsa_b200_decode_args* args) {
+  const int st = check_decode_args(args);
+  if (st != QSA_B200_OK) return st;
+  DecodeParams p;
+  fill_params(args, &p);
+  return workspace_for(p);
+}
+
+int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t workspace_bytes,
+                    qsa_b200_stream_t stream) {
+  int st = check_decode_args(args);
+  if (st != QSA_B200_OK) return st;
+  if (args->rows == 0) return QSA_B200_OK;
+  st = check_device();
+  if (st != QSA_B200_OK) return st;
+  DecodeParams p;
+  fill_params(args, &p);
+  p.err = device_error_word();
+  const int64_t need = workspace_for(p);
+  if (need > 0) {
+    if (!workspace || (int64_t)workspace_bytes < need) return QSA_B200_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return QSA_B200_ERR_MISALIGNED;
+    const int64_t n = (int64_t)p.rows * p.num_q_heads * p.num_chunks;
+    p.part_o = static_cast<float*>(workspace);
+    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((n * 128 * 4) + 255) / 256 * 256);
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool use_tc = args->kernel == QSA_B200_KERNEL_TC ||
+                      (args->kernel == QSA_B200_KERNEL_AUTO && tc_supports_group(p.group));
+  cudaError_t e = use_tc ? launch_decode_tc(p, s) : launch_decode_simt(p, s);
+  if (e != cudaSuccess) return QSA_B200_ERR_LAUNCH;
+  if (p.num_chunks > 1) {
+    e = launch_combine(p, s);
+    if (e != cudaSuccess) return QSA_B200_ERR_LAUNCH;
+  }
+  return QSA_B200_OK;
+}
+
+int qsa_b200_slots(const qsa_b200_decode_args* args, int64_t* slots, qsa_b200_stream_t stream) {
+  int st = check_index_args(args);
+  if (st != QSA_B200_OK) return st;
+  if (args->rows == 0 || args->topk == 0) return QSA_B200_OK;
+  if (!slots) return QSA_B200_ERR_NULL_POINTER;
+  if (reinterpret_cast<uintptr_t>(slots) & 7u) return QSA_B200_ERR_MISALIGNED;
+  st = check_device();
+  if (st != QSA_B200_OK) return st;
+  DecodeParams p;
+  fill_params(args, &p);
+  const cudaError_t e = launch_slots(p, slots, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? QSA_B200_OK : QSA_B200_ERR_LAUNCH;
+}
+
+void launch_qsa_cuda(const void* q, const void* k, const void* v, const void* indices, const void* btable,
+                     const int32_t* t2r, const void* gate, void* out, float softmax_scale, float v_scale,
+                     int32_t nblocks, int32_t nreqs, int32_t num_q_heads, int32_t num_kv_heads, int32_t topk,
+                     int32_t page_sz, int32_t max_pages, int32_t head_dim, int32_t group_sz,
+                     qsa_b200_stream_t stream) {
+  if (num_kv_heads < 1 || group_sz * num_kv_heads != num_q_heads || !t2r) {
+    t_last_status = QSA_B200_ERR_BAD_SHAPE;
+    return;
+  }
+  qsa_b200_decode_args a = {};
+  a.q = q;
+  a.k_cache = k;
+  a.v_cache = v;
+  a.indices = static_cast<const int32_t*>(indices);
+  a.counts = nullptr;
+  a.btable = static_cast<const int32_t*>(btable);
+  a.t2r = t2r;
+  a.gate = gate;
+  a.out = out;
+  // The reference passes k_scale * log2(e) / sqrt(D); the library takes the
+  // natural-log score scale and folds log2(e) itself.
+  a.softmax_scale = softmax_scale / 1.4426950408889634f;
+  a.k_scale = 1.0f;
+  a.v_scale = v_scale;
+  a.rows = nreqs;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.page_size = page_sz;
+  a.pages_per_req = max_pages;
+  a.num_reqs = nreqs;
+  a.num_pages = nblocks;
+  a.topk = topk;
+  a.indices_stride = (int64_t)topk + 1;
+  a.count_column = 1;
+  a.btable_stride = max_pages;
+  a.kernel = QSA_B200_KERNEL_AUTO;
+  // The reference shape (Top-K <= 512) needs no workspace; longer selections
+  // need the split workspace, which this allocation-free signature cannot take.
+  t_last_status = qsa_b200_workspace_bytes(&a) > 0 ? QSA_B200_ERR_WORKSPACE : qsa_b200_decode(&a, nullptr, 0, stream);
+}
+
+int qsa_b200_last_status(void) { return t_last_status; }
+
+int qsa_b200_device_error(int clear) {
+  int val = 0;
+  if (cudaMemcpyFromSymbol(&val, qsa::g_device_error, sizeof(int)) != cudaSuccess) return QSA_B200_ERR_LAUNCH;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(qsa::g_device_error, &zero, sizeof(int)) != cudaSuccess) return QSA_B200_ERR_LAUNCH;
+  }
+  return val;
+}
+
+}  // extern "C"

@@ -1,0 +1,233 @@
+// Device helpers shared by the qsa_b200 kernels (sm_100a only).
+//
+// * token decode: Top-K logical index -> block table -> physical K/V row;
+// * bounded mbarrier waits that report a timeout instead of hanging;
+// * thin inline-PTX wrappers for cp.async, proxy fences and tcgen05
+//   (TMEM allocation, FP8 MMA, commit, TMEM loads).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+#include "qsa_internal.h"
+
+namespace qsa {
+
+constexpr int kHeadDim = 128;       // bytes per FP8 K/V row of one KV head
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------------------
+// Token decode (the bit-exact part of the path).
+//
+// row_request: the request whose block-table row a Top-K row reads
+//   (t2r[row], identity when t2r is NULL), or -1 when it is out of range.
+// row_count: how many leading columns of the Top-K row may be valid.
+// token_slot: physical token slot phys * P + t % P of column `col`, or -1
+//   when the entry is masked. A token is valid when
+//   * col < count                          (sm89_cuda.cu:113-115, :146)
+//   * t >= 0 and t / P < pages_per_req     (sm89_torch.py:31; sm89_cuda.cu:160)
+//   * 0 <= phys < num_pages                (sm89_torch.py:38; sm89_cuda.cu:164)
+// The K/V row of KV head g then starts (slot * Hkv + g) * 128 bytes into the
+// cache (sm89_torch.py:43; sm89_cuda.cu:165).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t row_request(const DecodeParams& p, int row) {
+  int64_t req = p.t2r ? (int64_t)__ldg(p.t2r + row) : (int64_t)row;
+  return (req >= 0 && req < p.num_reqs) ? req : -1;
+}
+
+__device__ __forceinline__ int row_count(const DecodeParams& p, int row) {
+  int c = p.topk;
+  if (p.counts) {
+    c = __ldg(p.counts + row);
+  } else if (p.count_column) {
+    c = __ldg(p.indices + (int64_t)row * p.indices_stride + p.topk);
+  }
+  return c < 0 ? 0 : (c > p.topk ? p.topk : c);
+}
+
+__device__ __forceinline__ int64_t token_slot(const DecodeParams& p, int row, int64_t req, int count, int col) {
+  if (req < 0 || col >= count) return -1;
+  const int t = __ldg(p.indices + (int64_t)row * p.indices_stride + col);
+  if (t < 0) return -1;
+  int lp, po;
+  if (p.page_shift >= 0) {
+    lp = t >> p.page_shift;
+    po = t & ((1 << p.page_shift) - 1);
+  } else {
+    lp = t / p.page_size;
+    po = t - lp * p.page_size;
+  }
+  if (lp >= p.pages_per_req) return -1;
+  const int64_t phys = (int64_t)__ldg(p.btable + req * p.btable_stride + lp);
+  if (phys < 0 || phys >= p.num_pages) return -1;
+  return phys * p.page_size + po;
+}
+
+// ---------------------------------------------------------------------------
+// Small PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+// 16-byte async copy global -> shared. src_bytes == 0 zero-fills the
+// destination without reading the source.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_dyn(int n) {
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    default: cp_async_wait<7>(); break;
+  }
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (the tensor core reads its operands through it).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with the given parity to complete. Gives up after about
+// `limit_ns` nanoseconds of wall time and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > limit_ns) return false;
+  }
+}
+
+// --------------------------- tcgen05 wrappers ------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], FP8 E4M3 inputs, FP32 accumulate.
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on `bar` when every tcgen05 op this thread issued so far is done.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor for tcgen05 (SM100 format): start address,
+// leading/stride byte offsets (>> 4), version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f8f6f4 with E4M3 A and B, FP32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_e4m3(int m, int n, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                             // D format: F32
+         | (0u << 7) | (0u << 10)              // A, B format: E4M3
+         | ((a_mn_major ? 1u : 0u) << 15)      // A major
+         | ((b_mn_major ? 1u : 0u) << 16)      // B major
+         | ((uint32_t)(n >> 3) << 17)          // N / 8
+         | ((uint32_t)(m >> 4) << 24);         // M / 16
+}
+
+// Byte offset of (row r, byte c) inside a tile stored with the 128-byte
+// swizzle: 128-byte rows, 16-byte chunk index XOR (row % 8).
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c) {
+  return r * 128u + ((((c >> 4) ^ (r & 7u)) << 4) | (c & 15u));
+}
+
+// FP8 helpers (CUDA's own conversion intrinsics).
+__device__ __forceinline__ uint8_t f32_to_e4m3(float x) {
+  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+  return __half2float(__half(h));
+}
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint16_t b2) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)b2, __NV_E4M3);
+  return __half22float2(__half2(h));
+}
+
+// A kernel that gives up on a bounded wait ORs a code into the device error
+// word (DecodeParams::err); the host reads it with qsa_b200_device_error().
+__device__ __forceinline__ void report_error(const DecodeParams& p, int code) {
+  if (p.err) atomicOr(p.err, code);
+}
+
+}  // namespace qsa

@@ -1,0 +1,65 @@
+// Internal launch parameters shared by the C-ABI layer and the kernels.
+// Not part of the public interface (that is include/qsa_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace qsa {
+
+struct DecodeParams {
+  // Tensors (device pointers). Q, gate and out are contiguous [rows, Hq, 128]
+  // bf16; the caches are contiguous [num_pages, P, Hkv, 128] FP8 E4M3FN.
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* gate;
+  __nv_bfloat16* out;
+  const uint8_t* k;
+  const uint8_t* v;
+  const int32_t* indices;  // [rows, indices_stride]; the first topk columns are the Top-K list
+  const int32_t* counts;   // optional [rows]
+  const int32_t* btable;   // [num_reqs, btable_stride]; the first pages_per_req columns are used
+  const int32_t* t2r;      // optional [rows]
+
+  float score_scale_log2;  // softmax_scale * k_scale * log2(e)
+  float v_scale;
+
+  int rows;
+  int num_q_heads;
+  int num_kv_heads;
+  int group;  // num_q_heads / num_kv_heads
+  int page_size;
+  int page_shift;  // log2(page_size) when it is a power of two, else -1
+  int pages_per_req;
+  int num_reqs;
+  int64_t num_pages;
+  int topk;
+  int64_t indices_stride;
+  int count_column;  // count read from indices[row * stride + topk]
+  int64_t btable_stride;
+
+  // Split of each Top-K row into chunks of `chunk_tokens` (flash-decoding).
+  // With num_chunks == 1 the kernel writes `out` directly; otherwise it writes
+  // per-chunk partial results that qsa_combine merges.
+  int chunk_tokens;
+  int num_chunks;
+  float* part_o;    // [rows, Hq, num_chunks, 128] normalised partial outputs
+  float* part_lse;  // [rows, Hq, num_chunks] log2-sum-exp2 of each chunk (-inf if empty)
+
+  int* err;  // device error word of the current device
+};
+
+// Kernel launchers (return cudaGetLastError() of the launch).
+cudaError_t launch_decode_tc(const DecodeParams& p, cudaStream_t stream);
+cudaError_t launch_decode_simt(const DecodeParams& p, cudaStream_t stream);
+cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream);
+cudaError_t launch_slots(const DecodeParams& p, int64_t* slots, cudaStream_t stream);
+
+// Tokens per chunk and the group sizes of the tensor-core kernel.
+int tc_chunk_tokens();
+bool tc_supports_group(int group);
+
+// Largest group size (Hq / Hkv) the tensor-core kernel handles.
+constexpr int kMaxGroupTc = 16;
+
+}  // namespace qsa

@@ -1,0 +1,177 @@
+"""ctypes bindings of the C ABI (include/qsa_b200.h).
+
+This is the binding a Python maintainer of the reference would add to call
+``libqsa_b200.so`` the way the reference's CUDA library is meant to be called
+(``launch_qsa_cuda``, sm89_cuda.cu:232-253, "Shared library (for Python /
+PyTorch ctypes)", sm89_cuda.cu:21-22). Pointers are raw device addresses
+(``tensor.data_ptr()``); streams are ``torch.cuda.Stream.cuda_stream``
+integers.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from ctypes import c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+
+from ._lib import load_clib
+
+OK = 0
+ERR_NULL_POINTER = -1
+ERR_BAD_SHAPE = -2
+ERR_UNSUPPORTED = -3
+ERR_MISALIGNED = -4
+ERR_WORKSPACE = -5
+ERR_DEVICE = -6
+ERR_LAUNCH = -7
+ERR_KERNEL = -8
+
+KERNEL_AUTO = 0
+KERNEL_TC = 1
+KERNEL_SIMT = 2
+
+LOG2E = 1.4426950408889634
+
+# Names of every function include/qsa_b200.h declares.
+EXPORTED = (
+    "qsa_b200_workspace_bytes",
+    "qsa_b200_decode",
+    "qsa_b200_slots",
+    "launch_qsa_cuda",
+    "qsa_b200_last_status",
+    "qsa_b200_device_error",
+    "qsa_b200_status_string",
+    "qsa_b200_abi_version",
+)
+
+
+class DecodeArgs(ctypes.Structure):
+    """Mirror of ``qsa_b200_decode_args``."""
+
+    _fields_ = [
+        ("q", c_void_p),
+        ("k_cache", c_void_p),
+        ("v_cache", c_void_p),
+        ("indices", c_void_p),
+        ("counts", c_void_p),
+        ("btable", c_void_p),
+        ("t2r", c_void_p),
+        ("gate", c_void_p),
+        ("out", c_void_p),
+        ("softmax_scale", c_float),
+        ("k_scale", c_float),
+        ("v_scale", c_float),
+        ("rows", c_int32),
+        ("num_q_heads", c_int32),
+        ("num_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("page_size", c_int32),
+        ("pages_per_req", c_int32),
+        ("num_reqs", c_int32),
+        ("num_pages", c_int64),
+        ("topk", c_int32),
+        ("indices_stride", c_int64),
+        ("count_column", c_int32),
+        ("btable_stride", c_int64),
+        ("kernel", c_int32),
+    ]
+
+
+_configured = False
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library with argument / return types declared."""
+    global _configured
+    L = load_clib()
+    if not _configured:
+        P = ctypes.POINTER(DecodeArgs)
+        L.qsa_b200_workspace_bytes.argtypes = [P]
+        L.qsa_b200_workspace_bytes.restype = c_int64
+        L.qsa_b200_decode.argtypes = [P, c_void_p, c_size_t, c_void_p]
+        L.qsa_b200_decode.restype = c_int
+        L.qsa_b200_slots.argtypes = [P, c_void_p, c_void_p]
+        L.qsa_b200_slots.restype = c_int
+        L.launch_qsa_cuda.argtypes = [c_void_p] * 8 + [c_float, c_float] + [c_int32] * 9 + [c_void_p]
+        L.launch_qsa_cuda.restype = None
+        L.qsa_b200_last_status.argtypes = []
+        L.qsa_b200_last_status.restype = c_int
+        L.qsa_b200_device_error.argtypes = [c_int]
+        L.qsa_b200_device_error.restype = c_int
+        L.qsa_b200_status_string.argtypes = [c_int]
+        L.qsa_b200_status_string.restype = ctypes.c_char_p
+        L.qsa_b200_abi_version.argtypes = []
+        L.qsa_b200_abi_version.restype = c_int
+        _configured = True
+    return L
+
+
+def status_string(status: int) -> str:
+    return lib().qsa_b200_status_string(int(status)).decode()
+
+
+def _ptr(t):
+    return None if t is None else c_void_p(t.data_ptr())
+
+
+def make_args(q, k, v, btable, t2r, indices, gate, out, *, counts=None, softmax_scale=None,
+              k_scale=1.0, v_scale=1.0, topk=None, count_column=False, kernel=KERNEL_AUTO) -> DecodeArgs:
+    """Fills ``qsa_b200_decode_args`` from torch tensors (no checks: the C
+    side validates). ``q``/``gate``/``out`` may be None for ``slots``."""
+    a = DecodeArgs()
+    a.q, a.k_cache, a.v_cache = _ptr(q), _ptr(k), _ptr(v)
+    a.indices, a.counts, a.btable, a.t2r = _ptr(indices), _ptr(counts), _ptr(btable), _ptr(t2r)
+    a.gate, a.out = _ptr(gate), _ptr(out)
+    ref = q if q is not None else None
+    hd = ref.shape[2] if ref is not None else 128
+    a.softmax_scale = float(hd ** -0.5 if softmax_scale is None else softmax_scale)
+    a.k_scale = float(k_scale)
+    a.v_scale = float(v_scale)
+    a.rows = int(indices.shape[0])
+    a.num_q_heads = int(q.shape[1]) if q is not None else 1
+    a.num_kv_heads = int(k.shape[2]) if k is not None else 1
+    a.head_dim = int(hd)
+    a.page_size = int(k.shape[1]) if k is not None else 1
+    a.pages_per_req = int(btable.shape[1])
+    a.num_reqs = int(btable.shape[0])
+    a.num_pages = int(k.shape[0]) if k is not None else 1
+    a.topk = int(indices.shape[1] - (1 if count_column else 0) if topk is None else topk)
+    a.indices_stride = int(indices.stride(0))
+    a.count_column = 1 if count_column else 0
+    a.btable_stride = int(btable.stride(0))
+    a.kernel = int(kernel)
+    return a
+
+
+def workspace_bytes(args: DecodeArgs) -> int:
+    return int(lib().qsa_b200_workspace_bytes(ctypes.byref(args)))
+
+
+def decode(args: DecodeArgs, workspace=None, workspace_bytes_: int = 0, stream: int = 0) -> int:
+    """Calls ``qsa_b200_decode``; returns its status."""
+    ws = None if workspace is None else c_void_p(workspace.data_ptr())
+    return int(lib().qsa_b200_decode(ctypes.byref(args), ws, c_size_t(workspace_bytes_), c_void_p(stream)))
+
+
+def slots(args: DecodeArgs, out, stream: int = 0) -> int:
+    return int(lib().qsa_b200_slots(ctypes.byref(args), c_void_p(out.data_ptr()), c_void_p(stream)))
+
+
+def launch_qsa_cuda(q, k, v, indices, btable, t2r, gate, out, k_scale, v_scale, stream: int = 0) -> int:
+    """Calls the reference-compatible launcher exactly as the reference's own
+    ``main`` does (sm89_cuda.cu:369-385): log2-domain softmax scale, indices
+    with the count column, rows == nreqs. Returns qsa_b200_last_status()."""
+    L = lib()
+    hd = q.shape[2]
+    ss = (1.0 / math.sqrt(hd)) * k_scale * LOG2E
+    nreqs, max_pages = btable.shape
+    L.launch_qsa_cuda(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(indices), _ptr(btable), _ptr(t2r), _ptr(gate), _ptr(out),
+        c_float(ss), c_float(v_scale), c_int32(k.shape[0]), c_int32(nreqs), c_int32(q.shape[1]),
+        c_int32(k.shape[2]), c_int32(indices.shape[1] - 1), c_int32(k.shape[1]), c_int32(max_pages),
+        c_int32(hd), c_int32(q.shape[1] // k.shape[2]), c_void_p(stream))
+    return int(L.qsa_b200_last_status())
+
+
+def device_error(clear: bool = False) -> int:
+    return int(lib().qsa_b200_device_error(1 if clear else 0))

@@ -1,0 +1,123 @@
+"""The torch-callable operator contract of the reference's decode path.
+
+Three call shapes, matching the reference's own entry points:
+
+* ``run(q, k_fp8, v_fp8, k_scale, v_scale, btable, t2r, indices, gate)`` --
+  same positional order, argument meaning and result as the reference's
+  ``run`` (sm89_cutedsl.py:311-351): ``indices`` is ``[rows, topk + 1]`` with
+  the valid count in its last column, a new bf16 ``[rows, Hq, D]`` tensor is
+  returned and the call synchronises the device, as the reference does
+  (sm89_cutedsl.py:350).
+* ``launch(q, k, v, indices, btable, t2r, gate, out, k_scale, v_scale)`` --
+  the reference's Triton launcher (sm89_triton.py:118-142): same count-column
+  layout, caller-provided ``out``, asynchronous.
+* ``qsa_decode(...)`` -- the general form: ``indices`` ``[rows, K]`` padded
+  with -1 (the layout of the reference's eager path, sm89_torch.py:30), optional per-row
+  ``counts``, optional explicit ``softmax_scale`` and ``out``; asynchronous on
+  the current stream.
+
+Every call goes through ``torch.ops.qsa_b200.decode`` into the C ABI of
+``libqsa_b200.so``; CUDA tensors only, no CPU path.
+
+Semantics (identical for the three shapes). For row r, query head h and KV
+head g = h // (Hq // Hkv)::
+
+    out[r,h] = softmax_t(q[r,h] . K[slot_t, g] * k_scale * softmax_scale)
+               . V[slot_t, g] * v_scale  *  sigmoid(gate[r,h])
+
+with ``softmax_scale = D ** -0.5`` by default (sm89_torch.py:47) and
+``slot_t = btable[t2r[r], t // P] * P + t % P``. Entries with ``t < 0``,
+``t // P >= pages_per_req``, a block-table entry outside ``[0, num_pages)``
+or a column at or past the row's count are masked. A row whose ``t2r`` entry
+is out of range, or that has no valid entry, gives zeros (as the reference's
+``reference()`` does, sm89_cutedsl.py:93-106; the eager path would give NaN).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import capi
+from ._lib import load_torch_ops
+
+_KERNELS = {"auto": capi.KERNEL_AUTO, "tc": capi.KERNEL_TC, "simt": capi.KERNEL_SIMT}
+
+
+def _kernel_code(kernel) -> int:
+    if isinstance(kernel, int):
+        return kernel
+    try:
+        return _KERNELS[kernel]
+    except KeyError:
+        raise ValueError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}") from None
+
+
+def qsa_decode(q, k, v, k_scale, v_scale, btable, t2r, indices, gate, out=None, counts=None, *,
+               softmax_scale=None, count_column=False, topk=None, kernel="auto"):
+    """Sparse paged GQA FP8 decode attention with a sigmoid gate.
+
+    Args:
+        q, gate: bf16 ``[rows, Hq, 128]`` (contiguous).
+        k, v: FP8 E4M3FN ``[num_pages, P, Hkv, 128]`` (contiguous).
+        k_scale, v_scale: float dequantisation scales of the caches.
+        btable: int32 ``[num_reqs, pages_per_req]`` physical page ids.
+        t2r: int32 ``[rows]`` Top-K row -> block-table row, or None (identity).
+        indices: int32 ``[rows, K]`` logical token ids (negative = masked);
+            with ``count_column=True`` the last column holds the valid count.
+        out: optional bf16 output, shaped like ``q``.
+        counts: optional int32 ``[rows]`` valid-prefix lengths.
+        softmax_scale: score scale (default ``D ** -0.5``).
+        topk: number of index columns to read (default: all but the count
+            column).
+        kernel: "auto" (default), "tc" (tensor-core kernel) or "simt"
+            (CUDA-core kernel, any group size).
+
+    Returns ``out``. Runs asynchronously on the current CUDA stream.
+    """
+    ops = load_torch_ops()
+    if out is None:
+        out = torch.empty_like(q)
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(q.shape[-1])
+    if topk is None:
+        topk = indices.shape[1] - (1 if count_column else 0)
+    ops.decode(q, k, v, btable, t2r, indices, gate, counts, float(softmax_scale), float(k_scale),
+               float(v_scale), bool(count_column), int(topk), _kernel_code(kernel), out)
+    return out
+
+
+def run(q, k_fp8, v_fp8, k_scale, v_scale, btable, t2r, indices, gate):
+    """Drop-in for the reference's ``run`` (sm89_cutedsl.py:311-351)."""
+    out = torch.zeros_like(q)
+    qsa_decode(q, k_fp8, v_fp8, k_scale, v_scale, btable, t2r, indices, gate, out=out, count_column=True)
+    torch.cuda.synchronize(q.device)
+    return out
+
+
+def launch(q, k, v, indices, btable, t2r, gate, out, k_scale, v_scale):
+    """Drop-in for the reference's Triton ``launch`` (sm89_triton.py:118-142)."""
+    return qsa_decode(q, k, v, k_scale, v_scale, btable, t2r, indices, gate, out=out, count_column=True)
+
+
+def slots(indices, btable, t2r, page_size, num_pages, counts=None, *, count_column=False, topk=None):
+    """Physical token slot of every Top-K entry (int64 ``[rows, topk]``, -1
+    where masked) -- the index decode every kernel runs, exposed for the
+    bit-exact check (sm89_torch.py:30-39)."""
+    ops = load_torch_ops()
+    if topk is None:
+        topk = indices.shape[1] - (1 if count_column else 0)
+    out = torch.empty((indices.shape[0], topk), dtype=torch.int64, device=indices.device)
+    ops.slots(btable, t2r, indices, counts, bool(count_column), int(topk), int(page_size), int(num_pages), out)
+    return out
+
+
+def workspace_bytes(rows, num_q_heads, topk) -> int:
+    """Device workspace one call needs (the split of Top-K rows longer than
+    512 entries into 512-entry chunks; 0 otherwise)."""
+    chunks = 1 if topk <= 512 else -(-topk // 512)
+    if chunks == 1:
+        return 0
+    n = rows * num_q_heads * chunks
+    return -(-(n * 128 * 4) // 256) * 256 + -(-(n * 4) // 256) * 256

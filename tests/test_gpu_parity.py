@@ -1,0 +1,359 @@
+"""GPU parity of the CUDA path against the oracle and the reference's own
+golden outputs. Every decode here runs the sm_100a kernels of
+libqsa_b200.so (through torch.ops.qsa_b200 or the C ABI directly)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_CASES
+from gpu_helpers import ATOL, RTOL, bits, check_close, compact_subset, max_ulps, np_to_dev, oracle_subset, u8
+from oracle import qsa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+KERNELS = ["tc", "simt"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import qsa_b200  # noqa: F401
+    from qsa_b200 import capi
+
+    capi.device_error(clear=True)
+    yield
+    torch.cuda.synchronize()
+    assert capi.device_error() == 0, "a kernel reported a device-side timeout"
+
+
+def _decode(d, kernel, counts=True, **kw):
+    from qsa_b200 import qsa_decode
+
+    out = qsa_decode(d["q"], d["k"], d["v"], d["k_scale"], d["v_scale"], d["btable"], d["t2r"], d["indices"],
+                     d["gate"], counts=d["counts"] if counts else None, kernel=kernel, **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+def _oracle_np(z, counts=True, **kw):
+    return O.attention(z["q"], z["k"], z["v"], float(z["k_scale"]), float(z["v_scale"]), z["btable"], z["t2r"],
+                       z["indices"], z["gate"], counts=z["counts"] if counts else None, **kw)
+
+
+# ---------------------------------------------------------------- golden ----
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_golden_vs_reference_outputs(golden, name, kernel):
+    """CUDA path vs the reference's own outputs on its seeded inputs."""
+    z = golden[name]
+    d = np_to_dev(z)
+    if "out_loop" in z:
+        out = _decode(d, kernel, counts=True)
+        check_close(bits(out), O.bf16_to_f32(z["out_loop"]), what=f"{name}/{kernel} vs reference()")
+    out = _decode(d, kernel, counts=False)
+    ref = O.bf16_to_f32(z["out_eager"]).astype(np.float64)
+    # the eager rule makes an empty row NaN, the CUDA path makes it 0
+    empty = np.isnan(ref).all(axis=(1, 2))
+    assert np.all(bits(out)[empty] == 0)
+    check_close(bits(out)[~empty], ref[~empty], what=f"{name}/{kernel} vs torch_eager")
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_golden_vs_oracle_tight(golden, name, kernel):
+    """Beyond the 2e-2 gate: within 2 bf16 ulps of the float64 oracle."""
+    z = golden[name]
+    out = _decode(np_to_dev(z), kernel, counts=True)
+    assert max_ulps(bits(out), _oracle_np(z)) <= 2.0
+
+
+def test_kat_closed_form_through_run(golden):
+    """sm89_cuda.cu:347-399: q = gate = 0, K = V = 1.0, scales 0.1 -> bf16(0.05)
+    everywhere, through the reference-shaped ``run`` (count column)."""
+    from qsa_b200 import run
+
+    z = golden["kat"]
+    d = np_to_dev(z)
+    idx = torch.cat([d["indices"], d["counts"][:, None]], dim=1).contiguous()
+    out = run(d["q"], d["k"], d["v"], d["k_scale"], d["v_scale"], d["btable"], d["t2r"], idx, d["gate"])
+    assert np.all(bits(out) == O.kat_expected_bf16())
+
+
+# ------------------------------------------------------------ bit-exact -----
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_slots_bit_exact_golden(golden, name):
+    from qsa_b200 import slots
+
+    z = golden[name]
+    d = np_to_dev(z)
+    for counts in (None, d["counts"]):
+        got = slots(d["indices"], d["btable"], d["t2r"], 16, d["k"].shape[0], counts=counts).cpu().numpy()
+        want = O.decode_slots(z["indices"], z["btable"], z["t2r"], 16, z["k"].shape[0],
+                              counts=None if counts is None else z["counts"])
+        assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("cfg", [1, 2, 4])
+def test_slots_bit_exact_full_size(cfg):
+    from qsa_b200 import slots
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(cfg, "cuda", seed=3, rows=None if cfg != 4 else 64)
+    got = slots(w.indices, w.btable, w.t2r, w.meta["page"], w.k.shape[0]).cpu().numpy()
+    want = O.decode_slots(w.indices.cpu().numpy(), w.btable.cpu().numpy(), w.t2r.cpu().numpy(), w.meta["page"],
+                          w.k.shape[0])
+    assert np.array_equal(got, want)
+    del w
+    torch.cuda.empty_cache()
+
+
+# ------------------------------------------------------------ full size -----
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_headline_config_full(kernel):
+    """configs[1] at full size (256 x 32q/8kv x d128 x Top-K 512) vs the
+    oracle on every row."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(1, "cuda", seed=0)
+    out = qsa_decode(*w.args(), kernel=kernel)
+    torch.cuda.synchronize()
+    ref = O.attention(bits(w.q), u8(w.k).reshape(w.k.shape), u8(w.v).reshape(w.v.shape), 1.0, 1.0,
+                      w.btable.cpu().numpy(), w.t2r.cpu().numpy(), w.indices.cpu().numpy(), bits(w.gate))
+    err = check_close(bits(out), ref, what=f"configs[1]/{kernel}")
+    assert max_ulps(bits(out), ref) <= 2.0, err
+
+
+def test_headline_config_vs_reference_eager_on_gpu():
+    """CUDA path vs the reference's eager ATen sequence run on the
+    same GPU (fp32 accumulation) -- the north star's comparison."""
+    from oracle.eager_port import torch_eager_port
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(1, "cuda", seed=1)
+    out = qsa_decode(*w.args())
+    ref = torch_eager_port(*w.args()).float().cpu().numpy()
+    torch.cuda.synchronize()
+    check_close(bits(out), ref, what="configs[1] vs eager on GPU")
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_sparse_config_subset(kernel):
+    """configs[2] (context 8192, 131072 pages, scattered gathers) at full
+    size; the oracle checks 24 rows through a compact copy of their pages."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(2, "cuda", seed=0)
+    out = qsa_decode(*w.args(), kernel=kernel)
+    torch.cuda.synchronize()
+    rows = list(range(0, 256, 11))
+    check_close(bits(out[rows]), oracle_subset(w, rows), what=f"configs[2]/{kernel}")
+    del w, out
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_ragged_gqa8_split(kernel):
+    """configs[4] shape (Hq=64/Hkv=8, context 32768, ragged Top-K up to
+    2048 -> 4 chunks per row and the split combine) on a 12-request shard."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(4, "cuda", seed=0, row_ids=list(range(12)))
+    out = qsa_decode(*w.args(), kernel=kernel)
+    torch.cuda.synchronize()
+    rows = list(range(12))
+    ref = oracle_subset(w, rows)
+    check_close(bits(out), ref, what=f"configs[4]/{kernel}")
+    assert max_ulps(bits(out), ref) <= 2.0
+    del w, out
+    torch.cuda.empty_cache()
+
+
+# -------------------------------------------------------- shape coverage ----
+@pytest.mark.parametrize("hq,hkv,kernel", [
+    (8, 8, "tc"), (16, 8, "tc"), (32, 8, "tc"), (64, 8, "tc"), (128, 8, "tc"),
+    (24, 8, "simt"), (48, 8, "simt"), (32, 8, "simt"), (32, 4, "tc"), (32, 1, "simt"),
+])
+def test_group_sizes(hq, hkv, kernel):
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=hq + hkv, rows=6, hq=hq, hkv=hkv, ppr=12, topk=100, mode="sample")
+    out = qsa_decode(*w.args(), kernel=kernel)
+    torch.cuda.synchronize()
+    ref = oracle_subset(w, list(range(6)))
+    check_close(bits(out), ref, what=f"G={hq // hkv}/{kernel}")
+    assert max_ulps(bits(out), ref) <= 2.0
+
+
+@pytest.mark.parametrize("page", [1, 8, 12, 32, 64])
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_page_sizes(page, kernel):
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    ppr = max(1, 256 // page)
+    w = make_workload(0, "cuda", seed=page, rows=5, page=page, ppr=ppr, topk=min(200, ppr * page), mode="sample")
+    out = qsa_decode(*w.args(), kernel=kernel)
+    torch.cuda.synchronize()
+    check_close(bits(out), oracle_subset(w, list(range(5))), what=f"P={page}/{kernel}")
+
+
+@pytest.mark.parametrize("topk", [1, 5, 127, 128, 129, 511, 512, 513, 1000, 1537, 3000])
+def test_topk_lengths(topk):
+    """Tile and chunk boundaries, including the split into several chunks."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=topk, rows=3, ppr=200, topk=topk, mode="sample")
+    for kernel in KERNELS:
+        out = qsa_decode(*w.args(), kernel=kernel)
+        torch.cuda.synchronize()
+        check_close(bits(out), oracle_subset(w, [0, 1, 2]), what=f"topk={topk}/{kernel}")
+
+
+# ----------------------------------------------------- semantics / API ------
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_t2r_remap_and_invalid_rows(kernel):
+    """t2r permutes rows onto block-table rows; rows whose request id is out
+    of range come back as zeros."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=5, rows=6, ppr=8, topk=96, mode="sample")
+    t2r = torch.tensor([3, 0, -1, 5, 6, 1], dtype=torch.int32, device="cuda")
+    out = qsa_decode(w.q, w.k, w.v, 1.0, 1.0, w.btable, t2r, w.indices, w.gate, kernel=kernel)
+    torch.cuda.synchronize()
+    ref = O.attention(bits(w.q), u8(w.k).reshape(w.k.shape), u8(w.v).reshape(w.v.shape), 1.0, 1.0,
+                      w.btable.cpu().numpy(), t2r.cpu().numpy(), w.indices.cpu().numpy(), bits(w.gate))
+    check_close(bits(out), ref, what="t2r")
+    assert np.all(bits(out)[[2, 4]] == 0)
+
+
+def test_reference_shaped_entry_points(golden):
+    """``run`` and ``launch`` take the reference's [rows, topk+1] count-column
+    layout and k_scale/v_scale (sm89_cutedsl.py:311, sm89_triton.py:118)."""
+    from qsa_b200 import launch, run
+
+    z = golden["scales"]
+    d = np_to_dev(z)
+    idx = torch.cat([d["indices"], d["counts"][:, None]], dim=1).contiguous()
+    args = (d["q"], d["k"], d["v"], d["k_scale"], d["v_scale"], d["btable"], d["t2r"], idx, d["gate"])
+    ref = O.bf16_to_f32(z["out_loop"])
+    check_close(bits(run(*args)), ref, what="run")
+    out = torch.empty_like(d["q"])
+    launch(d["q"], d["k"], d["v"], idx, d["btable"], d["t2r"], d["gate"], out, d["k_scale"], d["v_scale"])
+    torch.cuda.synchronize()
+    check_close(bits(out), ref, what="launch")
+
+
+def test_c_abi_launch_qsa_cuda_drop_in(golden):
+    """The reference's own C-ABI signature, called the way its main() does
+    (log2-domain scale, count column, stream 0)."""
+    from qsa_b200 import capi
+
+    z = golden["edge"]
+    d = np_to_dev(z)
+    idx = torch.cat([d["indices"], d["counts"][:, None]], dim=1).contiguous()
+    out = torch.full_like(d["q"], 7.0)
+    st = capi.launch_qsa_cuda(d["q"], d["k"], d["v"], idx, d["btable"], d["t2r"], d["gate"], out,
+                              d["k_scale"], d["v_scale"])
+    torch.cuda.synchronize()
+    assert st == capi.OK, capi.status_string(st)
+    check_close(bits(out), O.bf16_to_f32(z["out_loop"]), what="launch_qsa_cuda")
+
+
+def test_c_abi_decode_direct_with_workspace():
+    """qsa_b200_decode through ctypes on a split shape: the caller supplies
+    the workspace the library sizes; too small a workspace is refused."""
+    from qsa_b200 import capi
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=9, rows=4, ppr=100, topk=1200, mode="sample")
+    out = torch.empty_like(w.q)
+    a = capi.make_args(w.q, w.k, w.v, w.btable, w.t2r, w.indices, w.gate, out)
+    need = capi.workspace_bytes(a)
+    assert need > 0
+    small = torch.empty(need - 256, dtype=torch.uint8, device="cuda")
+    assert capi.decode(a, small, need - 256) == capi.ERR_WORKSPACE
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert capi.decode(a, ws, need, stream) == capi.OK
+    torch.cuda.synchronize()
+    check_close(bits(out), oracle_subset(w, [0, 1, 2, 3]), what="C ABI split")
+
+
+def test_strided_indices_and_btable():
+    """indices / block table with a row stride larger than their used width."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=11, rows=4, ppr=10, topk=120, mode="sample")
+    wide_idx = torch.full((4, 150), -1, dtype=torch.int32, device="cuda")
+    wide_idx[:, :120] = w.indices
+    wide_bt = torch.full((4, 16), -1, dtype=torch.int32, device="cuda")
+    wide_bt[:, :10] = w.btable
+    ref = qsa_decode(*w.args())
+    out = qsa_decode(w.q, w.k, w.v, 1.0, 1.0, wide_bt[:, :10], w.t2r, wide_idx[:, :130], w.gate, topk=120)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
+def test_duplicates_and_masked_entries_count_per_occurrence():
+    """Duplicate indices each count once (all implementations agree), and
+    masked entries contribute nothing."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=13, rows=2, ppr=4, topk=64)
+    idx = w.indices.clone()
+    idx[0, 10:20] = idx[0, 3]
+    idx[1, ::3] = -1
+    for kernel in KERNELS:
+        out = qsa_decode(w.q, w.k, w.v, 1.0, 1.0, w.btable, w.t2r, idx, w.gate, kernel=kernel)
+        torch.cuda.synchronize()
+        ref = O.attention(bits(w.q), u8(w.k).reshape(w.k.shape), u8(w.v).reshape(w.v.shape), 1.0, 1.0,
+                          w.btable.cpu().numpy(), w.t2r.cpu().numpy(), idx.cpu().numpy(), bits(w.gate))
+        check_close(bits(out), ref, what=f"dups/{kernel}")
+
+
+def test_cuda_graph_replay_matches_eager():
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(1, "cuda", seed=2, rows=64)
+    ref = qsa_decode(*w.args())
+    out = torch.empty_like(ref)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        qsa_decode(*w.args(), out=out)  # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    out.zero_()
+    with torch.cuda.graph(g):
+        qsa_decode(*w.args(), out=out)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    del g
+
+
+def test_errors_are_loud():
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=1)
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        qsa_decode(w.q.float(), w.k, w.v, 1.0, 1.0, w.btable, w.t2r, w.indices, w.gate)
+    with pytest.raises(RuntimeError, match="int32"):
+        qsa_decode(w.q, w.k, w.v, 1.0, 1.0, w.btable.long(), w.t2r, w.indices, w.gate)
+    with pytest.raises(RuntimeError):
+        qsa_decode(w.q, w.k, w.v, 1.0, 1.0, w.btable, w.t2r, w.indices[:2], w.gate)
