@@ -55,8 +55,8 @@ int* device_error_word() {
   return a;
 }
 
-int num_chunks_for(int topk) {
-  const int c = tc_chunk_tokens();
+int num_chunks_for(int topk, int group) {
+  const int c = tc_chunk_tokens(group);
   return topk <= c ? 1 : (topk + c - 1) / c;
 }
 
@@ -123,8 +123,8 @@ void fill_params(const qsa_b200_decode_args* a, DecodeParams* p) {
   p->indices_stride = a->indices_stride;
   p->count_column = a->count_column;
   p->btable_stride = a->btable_stride;
-  p->chunk_tokens = tc_chunk_tokens();
-  p->num_chunks = num_chunks_for(a->topk);
+  p->chunk_tokens = tc_chunk_tokens(p->group);
+  p->num_chunks = num_chunks_for(a->topk, p->group);
   p->part_o = nullptr;
   p->part_lse = nullptr;
   p->err = nullptr;

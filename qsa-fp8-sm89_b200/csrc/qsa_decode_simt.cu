@@ -12,6 +12,9 @@
 namespace qsa {
 namespace {
 
+// Query heads (warps) per CTA; larger groups spread over gridDim.z.
+constexpr int kSimtHeadsPerBlock = 8;
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -60,7 +63,9 @@ __global__ void qsa_decode_simt_kernel(DecodeParams p) {
   const int chunk = blockIdx.y;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int h = g * p.group + warp;
+  const int hg = blockIdx.z * kSimtHeadsPerBlock + warp;  // head within the group
+  if (hg >= p.group) return;                               // warp-uniform
+  const int h = g * p.group + hg;
 
   const int64_t req = row_request(p, row);
   const int count = row_count(p, row);
@@ -173,8 +178,10 @@ __global__ void qsa_slots_kernel(DecodeParams p, int64_t* slots) {
 }  // namespace
 
 cudaError_t launch_decode_simt(const DecodeParams& p, cudaStream_t stream) {
-  dim3 grid((unsigned)(p.rows * p.num_kv_heads), (unsigned)p.num_chunks, 1);
-  dim3 block((unsigned)(32 * p.group), 1, 1);
+  const int heads = p.group < kSimtHeadsPerBlock ? p.group : kSimtHeadsPerBlock;
+  dim3 grid((unsigned)(p.rows * p.num_kv_heads), (unsigned)p.num_chunks,
+            (unsigned)((p.group + kSimtHeadsPerBlock - 1) / kSimtHeadsPerBlock));
+  dim3 block((unsigned)(32 * heads), 1, 1);
   qsa_decode_simt_kernel<<<grid, block, 0, stream>>>(p);
   return cudaGetLastError();
 }

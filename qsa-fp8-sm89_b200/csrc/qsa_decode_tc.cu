@@ -1,31 +1,38 @@
-// Tensor-core decode kernel for sm_100a (tcgen05, FP8 operands, TMEM
-// accumulators).
+// Tensor-core decode kernel for sm_100a: persistent, warp-specialised, TMA
+// gather loads, FP8 tcgen05 MMAs with TMEM accumulators.
 //
-// One CTA (128 threads) serves one (row, KV head, chunk of up to 512 Top-K
-// entries). Every selected 128-byte K/V row is read from HBM once and shared
-// by the G query heads of the group.
+// Work item = (Top-K row, KV head, chunk of up to kTiles*128 Top-K entries).
+// Each CTA (one per SM) walks items blockIdx.x, blockIdx.x + gridDim.x, ...
+// with three roles that overlap across items:
 //
-// Layout of the work, per CTA:
-//   1. decode the chunk's Top-K entries to K/V row offsets (smem table);
-//   2. split each query head into four FP8 E4M3 terms,
-//        q * 2^E_h = t0 + t1/16 + t2/256 + t3/4096   (exact for bf16 q),
-//      stored as the N x 128 B operand Qs, row h*4+j = term j of head h;
-//   3. stream K tiles then V tiles (128 tokens x 128 B, 16 KB each) through a
-//      4-slot ring with 16-byte cp.async, written in the 128-byte-swizzled
-//      K-major layout the tensor core reads directly -- no dequantisation;
-//   4. S = K_tile . Qs^T on the tensor core (M=128 tokens, N = 4G padded to a
-//      multiple of 16, K=128 dims) into TMEM, one column block per tile;
-//   5. softmax over the whole chunk (two-pass: exact max and sum), the
-//      probabilities split into four FP8 terms of p*256 the same way and
-//      written as the operand Ps (row h*4+j, one byte per token);
-//   6. O^T = V_tile^T . Ps^T on the tensor core (V read MN-major from the same
-//      swizzled tile, M=128 dims, N as above, K=128 tokens), accumulated in
-//      TMEM across tiles;
-//   7. epilogue: recombine the terms, normalise, v_scale, sigmoid gate, bf16
-//      store (or a normalised partial + log-sum-exp for the split combine).
+//   warp 0  loader   decodes the item's Top-K entries (index -> block table
+//                    -> K/V row), splits the G query heads into FP8 terms
+//                    (operand Qs), and gathers the K tiles then the V tiles
+//                    (128 tokens x 128 B each) into a ring of shared-memory
+//                    slots with TMA tile::gather4 (4 rows per instruction,
+//                    128-byte swizzle, zero fill for masked rows);
+//   warp 1  MMA      one thread issues S = K_tile . Qs^T into TMEM for every
+//                    K tile of item i+1 before O^T += V_tile^T . Ps^T for
+//                    item i, so the tensor core never waits on a softmax;
+//   warps 2-5        softmax over the chunk's scores (exact max and sum),
+//                    probabilities as FP8 terms of p*256 (operand Ps), then
+//                    the epilogue: recombine, normalise, v_scale, sigmoid
+//                    gate, bf16 store (or a partial for the split combine).
 //
-// Every mbarrier wait is bounded; on a timeout the CTA records an error in the
-// device error word, drains its copies, frees its TMEM and returns.
+// Every selected 128-byte K/V row is read from HBM once and shared by the G
+// query heads. Q and P keep their precision through the term split:
+//   q * 2^E = t0 + t1/16 + t2/256 + t3/4096,   p * 256 = t0 + t1/16 + ...
+// with each term an E4M3 value, so the FP8 x FP8 tensor-core products are the
+// reference's fp32 products of the FP8 cache values with bf16 q / fp32 p.
+//
+// Synchronisation is by mbarriers: kv_full/kv_empty per ring slot, and
+// per item buffer (double-buffered TMEM and operands) q_full, meta_empty,
+// s_full, p_full, o_full, tmem_empty. Every wait is bounded; a CTA that gives
+// up records an error in the device error word, raises a CTA-wide abort
+// flag so the other roles leave their loops, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <atomic>
 
 #include "qsa_common.cuh"
@@ -33,13 +40,12 @@
 namespace qsa {
 namespace {
 
-constexpr int kTile = 128;           // tokens per tile
-constexpr int kTilesPerChunk = 4;    // tiles per CTA (512 tokens)
-constexpr int kStages = 4;           // K/V tile slots in shared memory
-constexpr int kThreads = 128;
-constexpr int kTileBytes = kTile * kHeadDim;  // 16 KiB
-constexpr int kTerms = 4;            // FP8 terms per Q / P value
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+constexpr int kTile = 128;                    // tokens per tile
+constexpr int kTileBytes = kTile * kHeadDim;  // 16 KiB of FP8
+constexpr int kTerms = 4;                     // FP8 terms per Q / P value
+constexpr int kThreads = 192;                 // loader, MMA, 4 softmax warps
+constexpr int kSmemLimit = 232448;            // 227 KiB opt-in per CTA
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr int kErrTimeout = 1;
 
 __host__ __device__ constexpr int pow2_at_least(int x) {
@@ -50,29 +56,95 @@ __host__ __device__ constexpr int pow2_at_least(int x) {
 
 template <int G>
 struct Cfg {
-  static constexpr int N = ((G * kTerms + 15) / 16) * 16;  // MMA N
-  static constexpr int kColS = 0;                           // S tile i at column i*N
-  static constexpr int kColO = kTilesPerChunk * N;          // O accumulator
-  static constexpr int kTmemCols = pow2_at_least(kColO + N);
-  // shared memory carve-up (offsets from a 1024-byte aligned base)
-  static constexpr int kRing = 0;
-  static constexpr int kQs = kRing + kStages * kTileBytes;
-  static constexpr int kPs = kQs + N * 128;
-  static constexpr int kRowOff = kPs + kTilesPerChunk * N * 128;
-  static constexpr int kRed = kRowOff + kTilesPerChunk * kTile * 8;   // float [4][G] (max) + [4][G] (sum)
-  static constexpr int kQinv = kRed + 2 * 4 * G * 4;                  // float [G]
-  static constexpr int kBars = ((kQinv + G * 4 + 7) / 8) * 8;         // uint64 [kStages + 2]
-  static constexpr int kTmemSlot = kBars + (kStages + 2) * 8;         // uint32
-  static constexpr int kBytes = kTmemSlot + 16;
-  // alignment slack; a CTA that needs all 512 TMEM columns asks for enough
-  // shared memory to be alone on its SM, so no second CTA waits in alloc
-  static constexpr int kSmemAlloc = (kTmemCols == 512 && kBytes + 1024 < 120 * 1024) ? 120 * 1024 : kBytes + 1024;
+  static constexpr int N = ((G * kTerms + 15) / 16) * 16;  // MMA N (rows of Qs / Ps)
+  static constexpr int kTiles = G <= 8 ? 4 : 2;             // tiles per item
+  static constexpr int kChunk = kTiles * kTile;             // Top-K entries per item
+  static constexpr int kBufCols = kTiles * N + N;           // S tiles + O, per buffer
+  static constexpr int kTmemCols = pow2_at_least(2 * kBufCols);
+  static constexpr int kQsBytes = N * 128;
+  static constexpr int kPsBytes = kTiles * N * 128;
+  // shared memory layout (offsets from a 1024-byte aligned base)
+  static constexpr int kQs = 0;                                 // [2][N][128]
+  static constexpr int kPs = kQs + 2 * kQsBytes;                // [2][kTiles][N][128]
+  static constexpr int kValid = kPs + 2 * kPsBytes;             // uint8 [2][kChunk]
+  static constexpr int kQinv = kValid + 2 * kChunk;             // float [2][G]
+  static constexpr int kRedMax = kQinv + 2 * G * 4;             // float [2][4][G]
+  static constexpr int kRedSum = kRedMax + 2 * 4 * G * 4;       // float [2][4][G]
+  static constexpr int kBars = ((kRedSum + 2 * 4 * G * 4 + 7) / 8) * 8;
+  static constexpr int kMaxSlots = 16;
+  static constexpr int kNumBars = 2 * kMaxSlots + 12;
+  static constexpr int kMisc = kBars + kNumBars * 8;            // tmem address, abort flag
+  static constexpr int kSlotBase = ((kMisc + 16 + 1023) / 1024) * 1024;
+  static constexpr int kSlots0 = (kSmemLimit - 1024 - kSlotBase) / kTileBytes;
+  static constexpr int kSlots = kSlots0 > kMaxSlots ? kMaxSlots : kSlots0;
+  static constexpr int kSmemAlloc = kSlotBase + kSlots * kTileBytes + 1024;
   static constexpr uint32_t kIdescS = idesc_e4m3(128, N, false, false);
   static constexpr uint32_t kIdescO = idesc_e4m3(128, N, true, false);
+  static_assert(kSlots >= 2 * kTiles, "ring must hold a K and a V chunk");
+  static_assert(kSmemAlloc <= kSmemLimit, "shared memory budget");
+  static_assert(kTmemCols <= 512, "TMEM budget");
 };
 
-// Split x (|x| < 448) into four E4M3 terms: x ~= t0 + t1/16 + t2/256 + t3/4096.
-__device__ __forceinline__ void split4(float x, uint8_t (&t)[4]) {
+struct Item {
+  int row, g, chunk;
+};
+
+__device__ __forceinline__ Item item_of(const DecodeParams& p, int item) {
+  Item it;
+  it.g = item % p.num_kv_heads;
+  const int rc = item / p.num_kv_heads;
+  it.chunk = rc % p.num_chunks;
+  it.row = rc / p.num_chunks;
+  return it;
+}
+
+__device__ __forceinline__ int item_tiles(const DecodeParams& p, int chunk, int chunk_tokens) {
+  const int c0 = chunk * chunk_tokens;
+  const int clen = max(0, min(chunk_tokens, p.topk - c0));
+  return (clen + kTile - 1) / kTile;
+}
+
+// ------------------------------------------------------------------ PTX ----
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// Four 128-byte rows (coordinates r0..r3 of a 2-D [rows, 128] byte tensor) into
+// 512 contiguous bytes of shared memory, 128-byte swizzled by address.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int r0, int r1,
+                                            int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Bounded wait that also gives up once another role raised the abort flag.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    uint64_t t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// Split x (|x| < 448) into E4M3 terms: x ~= t0 + t1/16 + t2/256 + t3/4096.
+__device__ __forceinline__ void split4(float x, uint8_t (&t)[kTerms]) {
 #pragma unroll
   for (int j = 0; j < kTerms; ++j) {
     t[j] = f32_to_e4m3(x);
@@ -80,9 +152,14 @@ __device__ __forceinline__ void split4(float x, uint8_t (&t)[4]) {
   }
 }
 
+__device__ __forceinline__ float combine4(const float* v) {
+  return v[0] + v[1] * 0.0625f + v[2] * 0.00390625f + v[3] * 0.000244140625f;
+}
+
 template <int G>
 __global__ void __launch_bounds__(kThreads, 1)
-qsa_decode_tc_kernel(DecodeParams p) {
+qsa_decode_tc_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
+                     const __grid_constant__ CUtensorMap tmap_v, int num_items) {
   using C = Cfg<G>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
@@ -92,176 +169,286 @@ qsa_decode_tc_kernel(DecodeParams p) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int g = blockIdx.x % p.num_kv_heads;
-  const int row = blockIdx.x / p.num_kv_heads;
-  const int chunk = blockIdx.y;
 
-  int64_t* rowoff = reinterpret_cast<int64_t*>(smem + C::kRowOff);
-  float* red_max = reinterpret_cast<float*>(smem + C::kRed);
-  float* red_sum = red_max + 4 * G;
-  float* qinv = reinterpret_cast<float*>(smem + C::kQinv);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBars);
-  uint64_t* bar_slot = bars;              // [kStages]: MMA finished reading slot
-  uint64_t* bar_s = bars + kStages;       // all S tiles computed
-  uint64_t* bar_o = bars + kStages + 1;   // O accumulation finished
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlot);
+  uint64_t* kv_full = bars;                       // [kSlots] loader tx -> MMA
+  uint64_t* kv_empty = bars + C::kMaxSlots;       // [kSlots] MMA commit -> loader
+  uint64_t* q_full = bars + 2 * C::kMaxSlots;     // [2] loader -> MMA
+  uint64_t* meta_empty = q_full + 2;              // [2] softmax -> loader
+  uint64_t* s_full = q_full + 4;                  // [2] MMA commit -> softmax
+  uint64_t* p_full = q_full + 6;                  // [2] softmax -> MMA
+  uint64_t* o_full = q_full + 8;                  // [2] MMA commit -> epilogue
+  uint64_t* tmem_empty = q_full + 10;             // [2] epilogue (128 arrivals) -> MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMisc + 8);
+  float* qinv = reinterpret_cast<float*>(smem + C::kQinv);
+  float* red_max = reinterpret_cast<float*>(smem + C::kRedMax);
+  float* red_sum = reinterpret_cast<float*>(smem + C::kRedSum);
+  uint8_t* valid = smem + C::kValid;
 
-  const uint32_t ring_s = base_s + C::kRing;
-  const uint32_t qs_s = base_s + C::kQs;
-  const uint32_t ps_s = base_s + C::kPs;
-
-  // ---- set-up: barriers, TMEM ------------------------------------------------
   if (tid == 0) {
-    for (int i = 0; i < kStages + 2; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < C::kSlots; ++i) {
+      mbar_init(kv_full + i, 1);
+      mbar_init(kv_empty + i, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(q_full + b, 1);
+      mbar_init(meta_empty + b, 1);
+      mbar_init(s_full + b, 1);
+      mbar_init(p_full + b, 1);
+      mbar_init(o_full + b, 1);
+      mbar_init(tmem_empty + b, 128);
+    }
+    *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
     tc_fence_before();
   }
-
-  // ---- 1. decode the chunk's Top-K entries -----------------------------------
-  const int64_t req = row_request(p, row);
-  const int count = row_count(p, row);
-  const int c0 = chunk * p.chunk_tokens;
-  const int clen = max(0, min(p.chunk_tokens, p.topk - c0));
-  const int ntiles = (clen + kTile - 1) / kTile;
-  int mine_valid = 0;
-  for (int i = tid; i < ntiles * kTile; i += kThreads) {
-    const int64_t slot = (i < clen) ? token_slot(p, row, req, count, c0 + i) : -1;
-    rowoff[i] = slot >= 0 ? (slot * p.num_kv_heads + g) * kHeadDim : -1;
-    mine_valid |= slot >= 0;
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_k);
+    prefetch_tmap(&tmap_v);
   }
-
-  // ---- 2. query split into FP8 terms (warp w: heads w, w+4, ...) --------------
-  for (int h = warp; h < G; h += 4) {
-    const int64_t qoff = ((int64_t)row * p.num_q_heads + g * G + h) * kHeadDim + lane * 4;
-    const uint2 raw = *reinterpret_cast<const uint2*>(p.q + qoff);
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-    const float x[4] = {a.x, a.y, b.x, b.y};
-    float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    // 2^E maps the head's largest |q| into [128, 256).
-    int e = 0;
-    if (amax > 0.f && amax <= 3.0e38f) {
-      const int ex = (int)((__float_as_uint(amax) >> 23) & 0xff) - 127;
-      e = min(max(7 - ex, -120), 120);
-    }
-    const float sc = __uint_as_float((uint32_t)(127 + e) << 23);
-    uint32_t packed[kTerms] = {0u, 0u, 0u, 0u};
-#pragma unroll
-    for (int d = 0; d < 4; ++d) {
-      uint8_t t[kTerms];
-      split4(x[d] * sc, t);
-#pragma unroll
-      for (int j = 0; j < kTerms; ++j) packed[j] |= (uint32_t)t[j] << (8 * d);
-    }
-#pragma unroll
-    for (int j = 0; j < kTerms; ++j)
-      *reinterpret_cast<uint32_t*>(smem + C::kQs + sw128_offset(h * kTerms + j, lane * 4)) = packed[j];
-    if (lane == 0) qinv[h] = __uint_as_float((uint32_t)(127 - e) << 23) * p.score_scale_log2;
-  }
-  // zero the padding rows of Qs and Ps (rows 4G .. N-1)
-  constexpr int kPadRows = C::N - G * kTerms;
-  if (kPadRows > 0) {
-    for (int i = tid; i < kPadRows * 8; i += kThreads) {
-      const int r = G * kTerms + i / 8;
-      const int ch = i % 8;
-      *reinterpret_cast<uint4*>(smem + C::kQs + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
-      for (int t = 0; t < kTilesPerChunk; ++t)
-        *reinterpret_cast<uint4*>(smem + C::kPs + t * C::N * 128 + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
-    }
-  }
-  fence_proxy_async_smem();
-  const int any_valid = __syncthreads_or(mine_valid);
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
 
-  if (any_valid) {
-    // ---- 3. start streaming: stream tile s < ntiles is K tile s, else V tile s-ntiles
-    auto issue_tile = [&](int s) {
-      const uint8_t* src_base = s < ntiles ? p.k : p.v;
-      const int tile = s < ntiles ? s : s - ntiles;
-      const uint32_t dst = ring_s + (uint32_t)(s % kStages) * kTileBytes;
-#pragma unroll
-      for (int it = 0; it < kTileBytes / 16 / kThreads; ++it) {
-        const int idx = it * kThreads + tid;
-        const int r = idx >> 3;
-        const int ch = idx & 7;
-        const int64_t off = rowoff[tile * kTile + r];
-        const uint8_t* src = off >= 0 ? src_base + off + ch * 16 : src_base;
-        cp_async_16(dst + sw128_offset(r, ch * 16), src, off >= 0 ? 16u : 0u);
-      }
-    };
-    const int nstream = 2 * ntiles;
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) {
-      if (s < nstream) issue_tile(s);
-      cp_async_commit();
-    }
+  if (warp == 0) {
+    // =============================== loader =================================
+    int t = 0;  // ring position of the next tile
+    for (int it = 0, item = blockIdx.x; item < num_items; ++it, item += gridDim.x) {
+      const Item w = item_of(p, item);
+      const int b = it & 1;
+      const int ub = it >> 1;
+      const int c0 = w.chunk * C::kChunk;
+      const int ntiles = item_tiles(p, w.chunk, C::kChunk);
+      const int64_t req = row_request(p, w.row);
+      const int count = row_count(p, w.row);
 
-    // ---- 4. K phase: S_j = K_j . Qs^T ---------------------------------------
-    for (int j = 0; j < ntiles; ++j) {
-      cp_async_wait<kStages - 1>();
-      fence_proxy_async_smem();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        const uint32_t a0 = ring_s + (uint32_t)(j % kStages) * kTileBytes;
+      // rows of this lane's 4 tokens in every tile: (slot * Hkv + g), -1 = masked
+      int coord[C::kTiles][4];
 #pragma unroll
-        for (int kk = 0; kk < kHeadDim / 32; ++kk) {
-          const uint64_t ad = smem_desc_sw128(a0 + kk * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(qs_s + kk * 32, 16, 1024);
-          mma_f8(tmem + C::kColS + j * C::N, ad, bd, C::kIdescS, kk > 0 ? 1u : 0u);
+      for (int j = 0; j < C::kTiles; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = j * kTile + lane * 4 + e;
+          const int64_t slot = (j < ntiles && c0 + i < p.topk) ? token_slot(p, w.row, req, count, c0 + i) : -1;
+          coord[j][e] = slot >= 0 ? (int)(slot * p.num_kv_heads + w.g) : -1;
         }
-        mma_commit(bar_slot + (j % kStages));
-        if (j == ntiles - 1) mma_commit(bar_s);
-      }
-      if (j + kStages < nstream) {
-        // the slot is refilled only once the MMA that read it has finished
-        const bool ok = mbar_wait_bounded(bar_slot + (j % kStages), (uint32_t)((j / kStages) & 1), kWaitLimitNs);
-        if (__syncthreads_or(!ok)) { failed = true; break; }
-        issue_tile(j + kStages);
-      }
-      cp_async_commit();
-    }
 
-    // ---- 5. softmax over the chunk ------------------------------------------
-    float sc[kTilesPerChunk][G];
-    float m_h[G], l_h[G];
-    if (!failed) {
-      const bool ok = mbar_wait_bounded(bar_s, 0, kWaitLimitNs);
-      failed = __syncthreads_or(!ok);
-    }
-    if (!failed) {
-      tc_fence_after();
-      const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+      // query split into FP8 terms (lane owns dims 4*lane .. 4*lane+3)
+      uint32_t qpk[G][kTerms];
+      float qsc[G];
 #pragma unroll
-      for (int i = 0; i < kTilesPerChunk; ++i) {
-        if (i < ntiles) {
+      for (int h = 0; h < G; ++h) {
+        const int64_t qoff = ((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim + lane * 4;
+        const uint2 raw = *reinterpret_cast<const uint2*>(p.q + qoff);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+        const float x[4] = {a.x, a.y, c.x, c.y};
+        float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        int e = 0;  // 2^e maps the head's largest |q| into [128, 256)
+        if (amax > 0.f && amax <= 3.0e38f) {
+          const int ex = (int)((__float_as_uint(amax) >> 23) & 0xff) - 127;
+          e = min(max(7 - ex, -120), 120);
+        }
+        const float sc = __uint_as_float((uint32_t)(127 + e) << 23);
+#pragma unroll
+        for (int j = 0; j < kTerms; ++j) qpk[h][j] = 0u;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+          uint8_t tt[kTerms];
+          split4(x[d] * sc, tt);
+#pragma unroll
+          for (int j = 0; j < kTerms; ++j) qpk[h][j] |= (uint32_t)tt[j] << (8 * d);
+        }
+        qsc[h] = __uint_as_float((uint32_t)(127 - e) << 23) * p.score_scale_log2;
+      }
+
+      // per-item operands go to buffer b once the softmax of item it-2 is done
+      if (ub > 0 && !__all_sync(0xffffffffu, wait_or_abort(meta_empty + b, (uint32_t)((ub - 1) & 1), abort_flag))) {
+        failed = true;
+        break;
+      }
+      uint8_t* qs = smem + C::kQs + b * C::kQsBytes;
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+#pragma unroll
+        for (int j = 0; j < kTerms; ++j)
+          *reinterpret_cast<uint32_t*>(qs + sw128_offset(h * kTerms + j, lane * 4)) = qpk[h][j];
+      for (int r = G * kTerms; r < C::N; ++r)  // zero padding rows of Qs
+        *reinterpret_cast<uint32_t*>(qs + r * 128 + lane * 4) = 0u;
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        if (lane == h) qinv[b * G + h] = qsc[h];
+#pragma unroll
+      for (int j = 0; j < C::kTiles; ++j) {
+        const uint32_t vb = (coord[j][0] >= 0 ? 1u : 0u) | (coord[j][1] >= 0 ? 0x100u : 0u) |
+                            (coord[j][2] >= 0 ? 0x10000u : 0u) | (coord[j][3] >= 0 ? 0x1000000u : 0u);
+        *reinterpret_cast<uint32_t*>(valid + b * C::kChunk + j * kTile + lane * 4) = vb;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_full + b);
+
+      // K tiles then V tiles of the item into the ring
+#pragma unroll
+      for (int s = 0; s < 2 * C::kTiles; ++s) {
+        if (s < 2 * ntiles) {
+          const int slot = t % C::kSlots;
+          const int use = t / C::kSlots;
+          if (use > 0 && !__all_sync(0xffffffffu, wait_or_abort(kv_empty + slot, (uint32_t)((use - 1) & 1), abort_flag))) {
+            failed = true;
+            break;
+          }
+          if (lane == 0) mbar_arrive_expect_tx(kv_full + slot, kTileBytes);
+          __syncwarp();
+          const int j = s < ntiles ? s : s - ntiles;
+          const CUtensorMap* map = s < ntiles ? &tmap_k : &tmap_v;
+          const uint32_t dst = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes + (uint32_t)lane * 512u;
+          int r[4] = {-1, -1, -1, -1};
+#pragma unroll
+          for (int jj = 0; jj < C::kTiles; ++jj)
+            if (jj == j) {
+              r[0] = coord[jj][0];
+              r[1] = coord[jj][1];
+              r[2] = coord[jj][2];
+              r[3] = coord[jj][3];
+            }
+          tma_gather4(dst, map, kv_full + slot, r[0], r[1], r[2], r[3]);
+          ++t;
+        }
+      }
+      if (failed) break;
+    }
+  } else if (warp == 1) {
+    // ================================= MMA ==================================
+    if (lane == 0) {
+      int t = 0;           // ring position of the next K tile
+      int prev_v = 0;      // ring position of the previous item's first V tile
+      int prev_tiles = 0;  // tiles of the previous item
+      int prev_it = -1;
+      auto issue_o = [&](int jt, int vpos, int ntiles) -> bool {
+        const int b = jt & 1;
+        if (!wait_or_abort(p_full + b, (uint32_t)((jt >> 1) & 1), abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + b * C::kBufCols + C::kTiles * C::N;
+        for (int j = 0; j < ntiles; ++j) {
+          const int pos = vpos + j;
+          const int slot = pos % C::kSlots;
+          if (!wait_or_abort(kv_full + slot, (uint32_t)((pos / C::kSlots) & 1), abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t a0 = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes;
+          const uint32_t b0 = base_s + C::kPs + b * C::kPsBytes + j * C::N * 128;
+#pragma unroll
+          for (int kk = 0; kk < kTile / 32; ++kk) {
+            const uint64_t ad = smem_desc_sw128(a0 + kk * 32 * 128, kTileBytes, 1024);
+            const uint64_t bd = smem_desc_sw128(b0 + kk * 32, 16, 1024);
+            mma_f8(d, ad, bd, C::kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(kv_empty + slot);
+        }
+        mma_commit(o_full + b);
+        return true;
+      };
+      for (int it = 0, item = blockIdx.x; item < num_items; ++it, item += gridDim.x) {
+        const Item w = item_of(p, item);
+        const int b = it & 1;
+        const int ub = it >> 1;
+        const int ntiles = item_tiles(p, w.chunk, C::kChunk);
+        if (ub > 0 && !wait_or_abort(tmem_empty + b, (uint32_t)((ub - 1) & 1), abort_flag)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        if (!wait_or_abort(q_full + b, (uint32_t)(ub & 1), abort_flag)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t qs0 = base_s + C::kQs + b * C::kQsBytes;
+        for (int j = 0; j < ntiles; ++j) {
+          const int slot = t % C::kSlots;
+          if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kHeadDim / 32; ++kk) {
+            const uint64_t ad = smem_desc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(qs0 + kk * 32, 16, 1024);
+            mma_f8(tmem + b * C::kBufCols + j * C::N, ad, bd, C::kIdescS, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(kv_empty + slot);
+          ++t;
+        }
+        if (failed) break;
+        mma_commit(s_full + b);
+        const int vpos = t;  // this item's V tiles follow its K tiles
+        t += ntiles;
+        if (prev_it >= 0 && !issue_o(prev_it, prev_v, prev_tiles)) {
+          failed = true;
+          break;
+        }
+        prev_it = it;
+        prev_v = vpos;
+        prev_tiles = ntiles;
+      }
+      if (!failed && prev_it >= 0 && !issue_o(prev_it, prev_v, prev_tiles)) failed = true;
+    }
+  } else {
+    // ======================== softmax + epilogue (128 thr) ==================
+    const int q4 = warp & 3;        // TMEM lane quadrant of this warp
+    const int sw = warp - 2;        // 0..3
+    const int tk = q4 * 32 + lane;  // token within a tile / head dim in the epilogue
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    for (int it = 0, item = blockIdx.x; item < num_items; ++it, item += gridDim.x) {
+      const Item w = item_of(p, item);
+      const int b = it & 1;
+      const int ub = it >> 1;
+      const int ntiles = item_tiles(p, w.chunk, C::kChunk);
+
+      // gate of this thread's dim for every head, fetched early
+      float gate[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        gate[h] = __bfloat162float(p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim + tk]);
+
+      // q_full publishes the loader's validity bytes and query scales; s_full
+      // the scores. Once anything failed the group keeps walking its items
+      // (the named barriers must still match) but skips the tensor memory.
+      if (!failed) {
+        const bool ok = wait_or_abort(q_full + b, (uint32_t)(ub & 1), abort_flag) &&
+                        wait_or_abort(s_full + b, (uint32_t)(ub & 1), abort_flag);
+        failed = !__all_sync(0xffffffffu, ok);
+      }
+      tc_fence_after();
+      float sc[C::kTiles][G];
+#pragma unroll
+      for (int j = 0; j < C::kTiles; ++j) {
+        if (j < ntiles && !failed) {
           float v[C::N];
 #pragma unroll
           for (int cb = 0; cb < C::N; cb += 16) {
             float tmp[16];
-            tmem_ld16(tmem + lane_base + C::kColS + i * C::N + cb, tmp);
+            tmem_ld16(tmem + lane_base + b * C::kBufCols + j * C::N + cb, tmp);
             tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < 16; ++c) v[cb + c] = tmp[c];
           }
-          const bool valid = rowoff[i * kTile + tid] >= 0;
+          const bool ok = valid[b * C::kChunk + j * kTile + tk] != 0;
 #pragma unroll
-          for (int h = 0; h < G; ++h) {
-            const float s = v[h * 4] + v[h * 4 + 1] * 0.0625f + v[h * 4 + 2] * 0.00390625f +
-                            v[h * 4 + 3] * 0.000244140625f;
-            sc[i][h] = valid ? s * qinv[h] : -INFINITY;
-          }
+          for (int h = 0; h < G; ++h) sc[j][h] = ok ? combine4(v + h * kTerms) * qinv[b * G + h] : -INFINITY;
         } else {
 #pragma unroll
-          for (int h = 0; h < G; ++h) sc[i][h] = -INFINITY;
+          for (int h = 0; h < G; ++h) sc[j][h] = -INFINITY;
         }
       }
       // exact max per head over the chunk
@@ -269,132 +456,141 @@ qsa_decode_tc_kernel(DecodeParams p) {
       for (int h = 0; h < G; ++h) {
         float mx = sc[0][h];
 #pragma unroll
-        for (int i = 1; i < kTilesPerChunk; ++i) mx = fmaxf(mx, sc[i][h]);
+        for (int j = 1; j < C::kTiles; ++j) mx = fmaxf(mx, sc[j][h]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) red_max[warp * G + h] = mx;
+        if (lane == 0) red_max[(b * 4 + sw) * G + h] = mx;
       }
-      __syncthreads();
+      named_bar_sync(1, 128);
+      float m_h[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        m_h[h] = fmaxf(fmaxf(red_max[h], red_max[G + h]), fmaxf(red_max[2 * G + h], red_max[3 * G + h]));
+        const float* rm = red_max + b * 4 * G + h;
+        m_h[h] = fmaxf(fmaxf(rm[0], rm[G]), fmaxf(rm[2 * G], rm[3 * G]));
         float sum = 0.f;
 #pragma unroll
-        for (int i = 0; i < kTilesPerChunk; ++i) {
-          const float pr = (sc[i][h] == -INFINITY) ? 0.f : exp2f(sc[i][h] - m_h[h]);
-          sc[i][h] = pr;
+        for (int j = 0; j < C::kTiles; ++j) {
+          const float pr = sc[j][h] == -INFINITY ? 0.f : exp2f(sc[j][h] - m_h[h]);
+          sc[j][h] = pr;
           sum += pr;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) red_sum[warp * G + h] = sum;
+        if (lane == 0) red_sum[(b * 4 + sw) * G + h] = sum;
       }
-      // probabilities -> FP8 terms of p*256, one byte per token per row
+      // probabilities -> FP8 terms of p*256 (row h*4+j of Ps, one byte per token)
+      uint8_t* ps = smem + C::kPs + b * C::kPsBytes;
 #pragma unroll
-      for (int i = 0; i < kTilesPerChunk; ++i) {
-        if (i < ntiles) {
-          uint8_t* ps = smem + C::kPs + i * C::N * 128;
+      for (int j = 0; j < C::kTiles; ++j) {
+        if (j < ntiles) {
 #pragma unroll
           for (int h = 0; h < G; ++h) {
-            uint8_t t[kTerms];
-            split4(sc[i][h] * 256.0f, t);
+            uint8_t tt[kTerms];
+            split4(sc[j][h] * 256.0f, tt);
 #pragma unroll
-            for (int j = 0; j < kTerms; ++j) ps[sw128_offset(h * kTerms + j, tid)] = t[j];
+            for (int jj = 0; jj < kTerms; ++jj) ps[j * C::N * 128 + sw128_offset(h * kTerms + jj, tk)] = tt[jj];
           }
+          for (int r = G * kTerms; r < C::N; ++r) ps[j * C::N * 128 + sw128_offset(r, tk)] = 0;
         }
       }
       fence_proxy_async_smem();
-      __syncthreads();
-#pragma unroll
-      for (int h = 0; h < G; ++h)
-        l_h[h] = red_sum[h] + red_sum[G + h] + red_sum[2 * G + h] + red_sum[3 * G + h];
-
-      // ---- 6. V phase: O^T += V_j^T . Ps_j^T ----------------------------------
-      for (int jv = 0; jv < ntiles; ++jv) {
-        cp_async_wait_dyn(kStages - 1 - jv);
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-          tc_fence_after();
-          const int s = ntiles + jv;
-          const uint32_t a0 = ring_s + (uint32_t)(s % kStages) * kTileBytes;
-          const uint32_t b0 = ps_s + (uint32_t)(jv * C::N * 128);
-#pragma unroll
-          for (int kk = 0; kk < kTile / 32; ++kk) {
-            const uint64_t ad = smem_desc_sw128(a0 + kk * 32 * 128, kTileBytes, 1024);
-            const uint64_t bd = smem_desc_sw128(b0 + kk * 32, 16, 1024);
-            mma_f8(tmem + C::kColO, ad, bd, C::kIdescO, (jv > 0 || kk > 0) ? 1u : 0u);
-          }
-          if (jv == ntiles - 1) mma_commit(bar_o);
-        }
+      named_bar_sync(1, 128);
+      if (sw == 0 && lane == 0 && !failed) {
+        mbar_arrive(p_full + b);
+        mbar_arrive(meta_empty + b);
       }
-      const bool ok = mbar_wait_bounded(bar_o, 0, kWaitLimitNs);
-      failed = __syncthreads_or(!ok);
-    }
+      float l_h[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float* rs = red_sum + b * 4 * G + h;
+        l_h[h] = rs[0] + rs[G] + rs[2 * G] + rs[3 * G];
+      }
 
-    // ---- 7. epilogue: thread = head dim d ------------------------------------
-    if (!failed) {
+      // ---- epilogue: thread = head dim tk ----------------------------------
+      if (!failed) failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + b, (uint32_t)(ub & 1), abort_flag));
+      if (failed) continue;
       tc_fence_after();
-      const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
       float v[C::N];
 #pragma unroll
       for (int cb = 0; cb < C::N; cb += 16) {
         float tmp[16];
-        tmem_ld16(tmem + lane_base + C::kColO + cb, tmp);
+        tmem_ld16(tmem + lane_base + b * C::kBufCols + C::kTiles * C::N + cb, tmp);
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 16; ++c) v[cb + c] = tmp[c];
       }
-      const int d = tid;
+      tc_fence_before();
+      mbar_arrive(tmem_empty + b);
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float acc = v[h * 4] + v[h * 4 + 1] * 0.0625f + v[h * 4 + 2] * 0.00390625f +
-                          v[h * 4 + 3] * 0.000244140625f;
-        const float o = l_h[h] > 0.f ? acc * (1.0f / 256.0f) / l_h[h] : 0.f;
-        const int64_t off = ((int64_t)row * p.num_q_heads + g * G + h) * kHeadDim + d;
+        const float o = (ntiles > 0 && l_h[h] > 0.f) ? combine4(v + h * kTerms) * (1.0f / 256.0f) / l_h[h] : 0.f;
+        const int64_t hrow = (int64_t)w.row * p.num_q_heads + w.g * G + h;
         if (p.num_chunks == 1) {
-          const float gt = __bfloat162float(p.gate[off]);
-          p.out[off] = __float2bfloat16_rn(o * p.v_scale * (1.0f / (1.0f + expf(-gt))));
+          p.out[hrow * kHeadDim + tk] = __float2bfloat16_rn(o * p.v_scale * (1.0f / (1.0f + expf(-gate[h]))));
         } else {
-          const int64_t pidx = ((int64_t)row * p.num_q_heads + g * G + h) * p.num_chunks + chunk;
-          p.part_o[pidx * kHeadDim + d] = o;
-          if (d == 0) p.part_lse[pidx] = l_h[h] > 0.f ? m_h[h] + log2f(l_h[h]) : -INFINITY;
+          const int64_t pidx = hrow * p.num_chunks + w.chunk;
+          p.part_o[pidx * kHeadDim + tk] = o;
+          if (tk == 0) p.part_lse[pidx] = l_h[h] > 0.f ? m_h[h] + log2f(l_h[h]) : -INFINITY;
         }
       }
     }
   }
 
-  if (!any_valid) {
-    // no valid entry in this chunk: zeros (or an empty partial)
-    for (int i = tid; i < G * kHeadDim; i += kThreads) {
-      const int h = i / kHeadDim;
-      const int d = i % kHeadDim;
-      const int64_t off = ((int64_t)row * p.num_q_heads + g * G + h) * kHeadDim + d;
-      if (p.num_chunks == 1) {
-        p.out[off] = __float2bfloat16_rn(0.f);
-      } else {
-        const int64_t pidx = ((int64_t)row * p.num_q_heads + g * G + h) * p.num_chunks + chunk;
-        p.part_o[pidx * kHeadDim + d] = 0.f;
-        if (d == 0) p.part_lse[pidx] = -INFINITY;
-      }
-    }
+  if (failed) {
+    *abort_flag = 1;
+    report_error(p, kErrTimeout);
   }
-
-  if (failed && tid == 0) report_error(p, kErrTimeout);
-  // ---- teardown ---------------------------------------------------------------
-  cp_async_wait<0>();
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
+// ------------------------------------------------------------------ host ----
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::atomic<void*> fn{nullptr};
+  void* f = fn.load(std::memory_order_acquire);
+  if (!f) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn.store(f, std::memory_order_release);
+  }
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+}
+
+// The cache viewed as a 2-D byte tensor [num_pages * P * Hkv rows, 128]; one
+// box is one 128-byte row (gather4 moves four of them).
+bool encode_rows(CUtensorMap* map, const void* base, int64_t rows) {
+  auto fn = encode_fn();
+  if (!fn || rows <= 0 || rows > 0x7fffffffll) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim};
+  const cuuint32_t box[2] = {(cuuint32_t)kHeadDim, 1u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  static std::atomic<int> counts[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int c = counts[dev & 63].load(std::memory_order_acquire);
+  if (!c) {
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+    counts[dev & 63].store(c, std::memory_order_release);
+  }
+  return c;
+}
+
 template <int G>
 cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   using C = Cfg<G>;
-  // The shared-memory opt-in is per device; remember which devices have it.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -405,14 +601,20 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  dim3 grid((unsigned)(p.rows * p.num_kv_heads), (unsigned)p.num_chunks, 1);
-  qsa_decode_tc_kernel<G><<<grid, kThreads, C::kSmemAlloc, stream>>>(p);
+  const int64_t rows = p.num_pages * p.page_size * p.num_kv_heads;
+  CUtensorMap mk, mv;
+  if (!encode_rows(&mk, p.k, rows) || !encode_rows(&mv, p.v, rows)) return cudaErrorInvalidValue;
+  const int64_t items = (int64_t)p.rows * p.num_kv_heads * p.num_chunks;
+  if (items <= 0) return cudaSuccess;
+  if (items > 0x7fffffffll) return cudaErrorInvalidValue;
+  const int grid = (int)(items < sm_count() ? items : sm_count());
+  qsa_decode_tc_kernel<G><<<grid, kThreads, C::kSmemAlloc, stream>>>(p, mk, mv, (int)items);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-int tc_chunk_tokens() { return kTile * kTilesPerChunk; }
+int tc_chunk_tokens(int group) { return group <= 8 ? 4 * kTile : 2 * kTile; }
 
 bool tc_supports_group(int group) {
   return group == 1 || group == 2 || group == 4 || group == 8 || group == 16;

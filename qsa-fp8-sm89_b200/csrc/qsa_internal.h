@@ -55,8 +55,10 @@ cudaError_t launch_decode_simt(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_slots(const DecodeParams& p, int64_t* slots, cudaStream_t stream);
 
-// Tokens per chunk and the group sizes of the tensor-core kernel.
-int tc_chunk_tokens();
+// Top-K entries per work item for a GQA group size (both kernels split rows
+// the same way, so the workspace size depends only on the shape), and the
+// group sizes of the tensor-core kernel.
+int tc_chunk_tokens(int group);
 bool tc_supports_group(int group);
 
 // Largest group size (Hq / Hkv) the tensor-core kernel handles.

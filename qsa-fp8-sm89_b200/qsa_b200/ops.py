@@ -113,10 +113,17 @@ def slots(indices, btable, t2r, page_size, num_pages, counts=None, *, count_colu
     return out
 
 
-def workspace_bytes(rows, num_q_heads, topk) -> int:
-    """Device workspace one call needs (the split of Top-K rows longer than
-    512 entries into 512-entry chunks; 0 otherwise)."""
-    chunks = 1 if topk <= 512 else -(-topk // 512)
+def chunk_tokens(num_q_heads, num_kv_heads) -> int:
+    """Top-K entries one work item covers: 512 for GQA groups up to 8, 256
+    for larger groups (their score tiles fill more tensor memory)."""
+    return 512 if num_q_heads // num_kv_heads <= 8 else 256
+
+
+def workspace_bytes(rows, num_q_heads, num_kv_heads, topk) -> int:
+    """Device workspace one call needs: the per-chunk partial results when a
+    Top-K row spans more than one chunk (0 otherwise)."""
+    c = chunk_tokens(num_q_heads, num_kv_heads)
+    chunks = 1 if topk <= c else -(-topk // c)
     if chunks == 1:
         return 0
     n = rows * num_q_heads * chunks

@@ -118,10 +118,13 @@ def test_workspace_sizes():
 
     a = _args_cpu(topk=512, indices_stride=512)
     a.indices = a.btable = a.q = a.k_cache = a.v_cache = a.gate = a.out = ctypes.c_void_p(4096)
-    assert capi.workspace_bytes(a) == 0 == ops.workspace_bytes(4, 32, 512)
+    assert capi.workspace_bytes(a) == 0 == ops.workspace_bytes(4, 32, 8, 512)
     a.topk, a.indices_stride = 1100, 1101
     n = 4 * 32 * 3
-    assert capi.workspace_bytes(a) == n * 512 + n * 4 == ops.workspace_bytes(4, 32, 1100)  # n*4 is 256-aligned
+    assert capi.workspace_bytes(a) == n * 512 + n * 4 == ops.workspace_bytes(4, 32, 8, 1100)  # n*4 is 256-aligned
+    a.num_q_heads = 128  # group 16: 256-entry chunks
+    n = 4 * 128 * 5
+    assert capi.workspace_bytes(a) == n * 512 + n * 4 == ops.workspace_bytes(4, 128, 8, 1100)
 
 
 def test_torch_ops_register_and_refuse_cpu_tensors():
