@@ -44,7 +44,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch on the
 # bench workload, from the ncu capture summarised in profiles/ (None until
 # captured for the current kernel).
-NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): None}
+NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): 276_772_096}
 
 
 def parse():
