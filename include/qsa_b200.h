@@ -54,7 +54,8 @@ enum {
   QSA_B200_ERR_WORKSPACE = -5,    /* workspace missing or too small */
   QSA_B200_ERR_DEVICE = -6,       /* current device is not sm_100 */
   QSA_B200_ERR_LAUNCH = -7,       /* the CUDA launch itself failed */
-  QSA_B200_ERR_KERNEL = -8        /* a kernel reported a device-side failure */
+  QSA_B200_ERR_KERNEL = -8,       /* a kernel reported a device-side failure */
+  QSA_B200_ERR_TOO_LARGE = -9     /* qsa_b200_decode_noalloc: split scratch above its fixed maximum */
 };
 
 /* Kernel selection. AUTO picks the tensor-core kernel for group sizes
@@ -132,6 +133,28 @@ QSA_B200_API const char* qsa_b200_status_string(int status);
 
 /* QSA_B200_ABI_VERSION of the loaded library. */
 QSA_B200_API int qsa_b200_abi_version(void);
+
+/* Fixed split-K scratch of qsa_b200_decode_noalloc, per device: 32 MiB, room
+ * for rows * num_q_heads * chunks up to about 65,000 partials (for example
+ * 128 rows x 64 query heads x 4 chunks of 512 Top-K entries). */
+#define QSA_B200_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* Allocation-free qsa_b200_decode. This entry point has NO counterpart in
+ * the reference. It serves callers that cannot allocate device memory at
+ * call time: a runtime with a fixed device budget, a latency-critical loop,
+ * an FFI caller without an allocator.
+ *   - The split-K scratch is a file-scope device array of
+ *     QSA_B200_NOALLOC_SCRATCH_BYTES per device; the call makes no
+ *     cudaMalloc, cudaFree or other allocating call.
+ *   - Returns QSA_B200_ERR_TOO_LARGE, before touching the device, when
+ *     qsa_b200_workspace_bytes(args) exceeds that maximum; otherwise the
+ *     statuses and results of qsa_b200_decode.
+ *   - The first call on each device looks up the array's address
+ *     (cudaGetSymbolAddress) with that device current: make that first call
+ *     before any stream capture.
+ *   - Calls that overlap in time on one device (other streams or threads)
+ *     share the scratch and race; the caller serialises them. */
+QSA_B200_API int qsa_b200_decode_noalloc(const qsa_b200_decode_args* args, qsa_b200_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -157,6 +157,8 @@ const char* qsa_b200_status_string(int status) {
     case QSA_B200_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) part";
     case QSA_B200_ERR_LAUNCH: return "CUDA kernel launch failed";
     case QSA_B200_ERR_KERNEL: return "a kernel reported a device-side failure";
+    case QSA_B200_ERR_TOO_LARGE:
+      return "split scratch needed exceeds QSA_B200_NOALLOC_SCRATCH_BYTES (use qsa_b200_decode with a workspace)";
     default: return "unknown status";
   }
 }

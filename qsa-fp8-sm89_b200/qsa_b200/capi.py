@@ -25,6 +25,10 @@ ERR_WORKSPACE = -5
 ERR_DEVICE = -6
 ERR_LAUNCH = -7
 ERR_KERNEL = -8
+ERR_TOO_LARGE = -9
+
+# Fixed split scratch of qsa_b200_decode_noalloc (QSA_B200_NOALLOC_SCRATCH_BYTES).
+NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 KERNEL_AUTO = 0
 KERNEL_TC = 1
@@ -42,6 +46,7 @@ EXPORTED = (
     "qsa_b200_device_error",
     "qsa_b200_status_string",
     "qsa_b200_abi_version",
+    "qsa_b200_decode_noalloc",
 )
 
 
@@ -102,6 +107,8 @@ def lib() -> ctypes.CDLL:
         L.qsa_b200_status_string.restype = ctypes.c_char_p
         L.qsa_b200_abi_version.argtypes = []
         L.qsa_b200_abi_version.restype = c_int
+        L.qsa_b200_decode_noalloc.argtypes = [P, c_void_p]
+        L.qsa_b200_decode_noalloc.restype = c_int
         _configured = True
     return L
 
@@ -151,6 +158,12 @@ def decode(args: DecodeArgs, workspace=None, workspace_bytes_: int = 0, stream: 
     """Calls ``qsa_b200_decode``; returns its status."""
     ws = None if workspace is None else c_void_p(workspace.data_ptr())
     return int(lib().qsa_b200_decode(ctypes.byref(args), ws, c_size_t(workspace_bytes_), c_void_p(stream)))
+
+
+def decode_noalloc(args: DecodeArgs, stream: int = 0) -> int:
+    """Calls ``qsa_b200_decode_noalloc`` (split scratch from the library's
+    fixed device array, no workspace); returns its status."""
+    return int(lib().qsa_b200_decode_noalloc(ctypes.byref(args), c_void_p(stream)))
 
 
 def slots(args: DecodeArgs, out, stream: int = 0) -> int:
