@@ -55,7 +55,7 @@ enum {
   QSA_B200_ERR_DEVICE = -6,       /* current device is not sm_100 */
   QSA_B200_ERR_LAUNCH = -7,       /* the CUDA launch itself failed */
   QSA_B200_ERR_KERNEL = -8,       /* a kernel reported a device-side failure */
-  QSA_B200_ERR_TOO_LARGE = -9     /* qsa_b200_decode_noalloc: split scratch above its fixed maximum */
+  QSA_B200_ERR_TOO_LARGE = -9     /* workspace above the fixed scratch of qsa_b200_decode_noalloc */
 };
 
 /* Kernel selection. AUTO picks the tensor-core kernel for group sizes
@@ -90,12 +90,18 @@ typedef struct qsa_b200_decode_args {
   int32_t kernel;         /* QSA_B200_KERNEL_* */
 } qsa_b200_decode_args;
 
-/* Bytes of device workspace qsa_b200_decode needs (0 when topk <= 512:
- * one chunk per row, no split). Negative on invalid arguments. */
+/* Bytes of device workspace qsa_b200_decode needs, each part 256-byte
+ * aligned: the tensor-core kernel's row map (one int32 token slot per Top-K
+ * entry: rows x chunks x 512 entries, 256 for group 16), then, when a Top-K
+ * row spans more than one chunk, the split partial outputs and log-sum-exps.
+ * 0 only for the CUDA-core kernel without a split. Negative on invalid
+ * arguments. */
 QSA_B200_API int64_t qsa_b200_workspace_bytes(const qsa_b200_decode_args* args);
 
 /* The decode. `workspace` (256-byte aligned) must hold
- * qsa_b200_workspace_bytes(args) bytes; it may be NULL when that is 0.
+ * qsa_b200_workspace_bytes(args) bytes; it may be NULL when that is 0. The
+ * workspace needs no clearing and may be reused by the next call on the same
+ * stream.
  * Replaces launch_qsa_cuda (sm89_cuda.cu:232-301) / run (sm89_cutedsl.py:311). */
 QSA_B200_API int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t workspace_bytes,
                     qsa_b200_stream_t stream);
@@ -113,7 +119,10 @@ QSA_B200_API int qsa_b200_slots(const qsa_b200_decode_args* args, int64_t* slots
  * (k_scale * log2(e) / sqrt(head_dim)), rows == nreqs and t2r is required.
  * Returns void like the reference; the status of the call is available from
  * qsa_b200_last_status(). Rows with an out-of-range t2r entry or no valid
- * token are written as zeros (the reference leaves them unwritten). */
+ * token are written as zeros (the reference leaves them unwritten). This
+ * signature takes no workspace: the call runs as qsa_b200_decode_noalloc, on
+ * the library's fixed per-device scratch (QSA_B200_ERR_TOO_LARGE beyond it),
+ * so calls that overlap in time on one device race. */
 QSA_B200_API void launch_qsa_cuda(const void* q, const void* k, const void* v, const void* indices, const void* btable,
                      const int32_t* t2r, const void* gate, void* out, float softmax_scale, float v_scale,
                      int32_t nblocks, int32_t nreqs, int32_t num_q_heads, int32_t num_kv_heads, int32_t topk,
@@ -134,17 +143,17 @@ QSA_B200_API const char* qsa_b200_status_string(int status);
 /* QSA_B200_ABI_VERSION of the loaded library. */
 QSA_B200_API int qsa_b200_abi_version(void);
 
-/* Fixed split-K scratch of qsa_b200_decode_noalloc, per device: 32 MiB, room
- * for rows * num_q_heads * chunks up to about 65,000 partials (for example
- * 128 rows x 64 query heads x 4 chunks of 512 Top-K entries). */
+/* Fixed workspace of qsa_b200_decode_noalloc, per device: 32 MiB, room for
+ * the row map and split partials of, for example, 128 rows x 64 query heads x
+ * 4 chunks of 512 Top-K entries (18 MiB). */
 #define QSA_B200_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
 /* Allocation-free qsa_b200_decode. This entry point has NO counterpart in
  * the reference. It serves callers that cannot allocate device memory at
  * call time: a runtime with a fixed device budget, a latency-critical loop,
  * an FFI caller without an allocator.
- *   - The split-K scratch is a file-scope device array of
- *     QSA_B200_NOALLOC_SCRATCH_BYTES per device; the call makes no
+ *   - The workspace (row map and split partials) is a file-scope device
+ *     array of QSA_B200_NOALLOC_SCRATCH_BYTES per device; the call makes no
  *     cudaMalloc, cudaFree or other allocating call.
  *   - Returns QSA_B200_ERR_TOO_LARGE, before touching the device, when
  *     qsa_b200_workspace_bytes(args) exceeds that maximum; otherwise the

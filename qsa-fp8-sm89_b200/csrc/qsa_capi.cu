@@ -1,9 +1,12 @@
 // C ABI of libqsa_b200.so (declared in include/qsa_b200.h).
 //
 // Validates arguments, turns them into qsa::DecodeParams and launches the
-// decode kernel (tensor-core kernel for group sizes 1/2/4/8/16, CUDA-core
-// kernel otherwise), plus the split combine when a Top-K row is longer than
-// one 512-entry chunk. No entry point allocates, synchronises or traps.
+// decode: for the tensor-core kernel (group sizes 1/2/4/8/16) the row-map
+// kernel and then the decode kernel; otherwise the CUDA-core kernel; plus the
+// split combine when a Top-K row is longer than one chunk. Workspace layout
+// (each part 256-byte aligned): the row map (tensor-core kernel only), the
+// partial outputs and the partial log-sum-exps (split rows only). No entry
+// point allocates, synchronises or traps.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -127,14 +130,32 @@ void fill_params(const qsa_b200_decode_args* a, DecodeParams* p) {
   p->num_chunks = num_chunks_for(a->topk, p->group);
   p->part_o = nullptr;
   p->part_lse = nullptr;
+  p->rowmap = nullptr;
+  p->rowmap_stride = p->num_chunks * p->chunk_tokens;
   p->err = nullptr;
 }
 
-int64_t workspace_for(const DecodeParams& p) {
-  if (p.num_chunks <= 1) return 0;
-  const int64_t n = (int64_t)p.rows * p.num_q_heads * p.num_chunks;
-  const int64_t o_bytes = ((n * 128 * 4) + 255) / 256 * 256;
-  return o_bytes + (n * 4 + 255) / 256 * 256;
+bool uses_tc(const qsa_b200_decode_args* a, int group) {
+  return a->kernel == QSA_B200_KERNEL_TC || (a->kernel == QSA_B200_KERNEL_AUTO && tc_supports_group(group));
+}
+
+int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
+// Workspace parts: [row map][partial outputs][partial log-sum-exps].
+struct WorkspaceLayout {
+  int64_t rowmap_bytes, part_o_bytes, part_lse_bytes;
+  int64_t total() const { return rowmap_bytes + part_o_bytes + part_lse_bytes; }
+};
+
+WorkspaceLayout workspace_for(const DecodeParams& p, bool tc) {
+  WorkspaceLayout w{0, 0, 0};
+  if (tc) w.rowmap_bytes = align256((int64_t)p.rows * p.rowmap_stride * 4);
+  if (p.num_chunks > 1) {
+    const int64_t n = (int64_t)p.rows * p.num_q_heads * p.num_chunks;
+    w.part_o_bytes = align256(n * 128 * 4);
+    w.part_lse_bytes = align256(n * 4);
+  }
+  return w;
 }
 
 }  // namespace
@@ -158,7 +179,7 @@ const char* qsa_b200_status_string(int status) {
     case QSA_B200_ERR_LAUNCH: return "CUDA kernel launch failed";
     case QSA_B200_ERR_KERNEL: return "a kernel reported a device-side failure";
     case QSA_B200_ERR_TOO_LARGE:
-      return "split scratch needed exceeds QSA_B200_NOALLOC_SCRATCH_BYTES (use qsa_b200_decode with a workspace)";
+      return "workspace needed exceeds QSA_B200_NOALLOC_SCRATCH_BYTES (use qsa_b200_decode with a workspace)";
     default: return "unknown status";
   }
 }
@@ -168,7 +189,8 @@ int64_t qsa_b200_workspace_bytes(const qsa_b200_decode_args* args) {
   if (st != QSA_B200_OK) return st;
   DecodeParams p;
   fill_params(args, &p);
-  return workspace_for(p);
+  if (args->rows == 0) return 0;
+  return workspace_for(p, uses_tc(args, p.group)).total();
 }
 
 int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t workspace_bytes,
@@ -181,18 +203,21 @@ int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t wo
   DecodeParams p;
   fill_params(args, &p);
   p.err = device_error_word();
-  const int64_t need = workspace_for(p);
-  if (need > 0) {
-    if (!workspace || (int64_t)workspace_bytes < need) return QSA_B200_ERR_WORKSPACE;
+  const bool use_tc = uses_tc(args, p.group);
+  const WorkspaceLayout lay = workspace_for(p, use_tc);
+  if (lay.total() > 0) {
+    if (!workspace || (int64_t)workspace_bytes < lay.total()) return QSA_B200_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return QSA_B200_ERR_MISALIGNED;
-    const int64_t n = (int64_t)p.rows * p.num_q_heads * p.num_chunks;
-    p.part_o = static_cast<float*>(workspace);
-    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((n * 128 * 4) + 255) / 256 * 256);
+    char* ws = static_cast<char*>(workspace);
+    if (use_tc) p.rowmap = reinterpret_cast<int32_t*>(ws);
+    if (p.num_chunks > 1) {
+      p.part_o = reinterpret_cast<float*>(ws + lay.rowmap_bytes);
+      p.part_lse = reinterpret_cast<float*>(ws + lay.rowmap_bytes + lay.part_o_bytes);
+    }
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool use_tc = args->kernel == QSA_B200_KERNEL_TC ||
-                      (args->kernel == QSA_B200_KERNEL_AUTO && tc_supports_group(p.group));
-  cudaError_t e = use_tc ? launch_decode_tc(p, s) : launch_decode_simt(p, s);
+  cudaError_t e = use_tc ? launch_rowmap(p, s) : cudaSuccess;
+  if (e == cudaSuccess) e = use_tc ? launch_decode_tc(p, s) : launch_decode_simt(p, s);
   if (e != cudaSuccess) return QSA_B200_ERR_LAUNCH;
   if (p.num_chunks > 1) {
     e = launch_combine(p, s);
@@ -252,9 +277,9 @@ void launch_qsa_cuda(const void* q, const void* k, const void* v, const void* in
   a.count_column = 1;
   a.btable_stride = max_pages;
   a.kernel = QSA_B200_KERNEL_AUTO;
-  // The reference shape (Top-K <= 512) needs no workspace; longer selections
-  // need the split workspace, which this allocation-free signature cannot take.
-  t_last_status = qsa_b200_workspace_bytes(&a) > 0 ? QSA_B200_ERR_WORKSPACE : qsa_b200_decode(&a, nullptr, 0, stream);
+  // This signature takes no workspace: the row map (and any split partials)
+  // go to the library's fixed per-device scratch.
+  t_last_status = qsa_b200_decode_noalloc(&a, stream);
 }
 
 int qsa_b200_last_status(void) { return t_last_status; }

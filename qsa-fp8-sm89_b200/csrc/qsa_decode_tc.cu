@@ -1,32 +1,33 @@
-// Tensor-core decode kernel for sm_100a: persistent, warp-specialised,
-// register-staged gathers into swizzled shared memory, FP8 tcgen05 MMAs with
-// TMEM accumulators.
+// Tensor-core decode kernel for sm_100a: persistent, warp-specialised, TMA
+// gathers into swizzled shared memory, FP8 tcgen05 MMAs with TMEM accumulators.
+//
+// The index decode runs first, in its own small kernel (qsa_rowmap_kernel):
+// every Top-K entry becomes its physical token slot phys * P + t % P (or -1)
+// in a row map in the workspace, in parallel over the whole GPU. The decode
+// kernel then needs no dependent global reads of its own.
 //
 // Work item = (Top-K row, KV head, chunk of up to kTiles*128 Top-K entries).
 // Each CTA (one per SM) walks items blockIdx.x, blockIdx.x + gridDim.x, ...
-// with four roles that overlap across items:
+// (its k-th item is blockIdx.x + k * gridDim.x) with four roles that overlap
+// across items:
 //
-//   decoder (warp 0)   runs up to kMeta-1 items ahead: decodes the item's
-//                      Top-K entries (index -> block table -> K/V row) into a
-//                      row table, writes the validity bytes and the gate, and
-//                      splits the G query heads into FP8 terms (operand Qs)
-//                      with their scales -- one slot of a kMeta-deep
-//                      metadata ring. It also starts every selected K/V row
-//                      of the item on its way from HBM into L2. Its
-//                      global loads are pipelined two items deep with no
-//                      dependent chain: request id, count and index loads of
-//                      item i+2, block-table and query loads of item i+1 are
-//                      in flight while item i is finished;
-//   loaders            one warp per ring slot; an item occupies consecutive
-//                      ring positions (its K tiles, then its V tiles) and
-//                      loader L fills the positions that map to slot L, in
-//                      order: the tile's 128 rows of 128 B go through
-//                      registers with coalesced 16-byte loads into the slot,
-//                      stored in the 128-byte-swizzled layout the tensor core
-//                      reads (zeros for masked rows);
+//   decoder (warp 0)   for a kMeta-deep metadata ring: one TMA bulk copy brings
+//                      the item's chunk of the row map into the slot's row
+//                      table, and the G query heads are split into FP8 terms
+//                      (operand Qs) with their scales;
+//   loaders            the ring of 16 KiB tile slots is filled in the order
+//                      the MMA warp drains it: K tiles of item k, then V tiles
+//                      of item k-1. Slot s belongs to loader s % kLoaders, which
+//                      refills it in order. A tile is 128 rows of 128 B: each
+//                      lane issues one TMA tile::gather4 of four rows (the
+//                      cache viewed as a [rows, 128] byte tensor, row
+//                      slot * Hkv + g; a masked entry has row -1 and reads
+//                      zeros), which lands in the 128-byte-swizzled layout the
+//                      tensor core reads and completes the slot's transaction
+//                      count;
 //   MMA warp           one thread issues S = K_tile . Qs^T into TMEM for every
-//                      K tile of item i+1 before O^T += V_tile^T . Ps^T for
-//                      item i, so the tensor core never waits on a softmax;
+//                      K tile of item k, then O^T += V_tile^T . Ps^T for item
+//                      k-1 (its probabilities are ready by then);
 //   4 softmax warps    softmax over the chunk's scores (exact max and sum),
 //                      probabilities as FP8 terms of p*256 (operand Ps); then
 //                      the epilogue of the previous item (its O is complete
@@ -42,9 +43,13 @@
 //
 // Synchronisation is by mbarriers: kv_full/kv_empty per K/V ring slot,
 // meta_full/meta_empty per metadata slot, s_full/o_full/tmem_empty per TMEM
-// accumulator buffer (three), p_full per probability buffer (two). Every wait is bounded; a CTA
-// that gives up records an error in the device error word, raises a CTA-wide
-// abort flag so the other roles leave their loops, frees its TMEM and returns.
+// accumulator buffer (three), p_full per probability buffer (two). Every wait
+// is bounded; a CTA that gives up records an error in the device error word,
+// raises a CTA-wide abort flag so the other roles leave their loops, waits for
+// its own copies in flight, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <atomic>
 
 #include "qsa_common.cuh"
@@ -59,9 +64,16 @@ constexpr int kTermsP = 4;                    // FP8 terms per probability
 constexpr int kMeta = 4;                      // metadata ring depth (items)
 constexpr int kTmemBufs = 3;                  // TMEM accumulator buffers (items)
 constexpr int kDecoderWarp = 0;
+constexpr int kLoaders = 6;                   // loader warps 1 .. kLoaders
+constexpr int kMmaWarp = 1 + kLoaders;
+constexpr int kSoftmax0 = kMmaWarp + 1;       // 4 softmax / epilogue warps
+// 12 warps, one CTA per SM: up to 168 registers per thread (each SM
+// sub-partition has 16K registers and holds a quarter of the warps)
+constexpr int kThreads = 32 * (kSoftmax0 + 4);
 constexpr int kSmemLimit = 232448;            // 227 KiB opt-in per CTA
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr int kErrTimeout = 1;
+static_assert(kThreads % 128 == 0, "whole warpgroups, so the four sub-partitions hold equal shares");
 
 __host__ __device__ constexpr int align128(int x) { return (x + 127) / 128 * 128; }
 
@@ -77,52 +89,36 @@ struct Cfg {
   static constexpr int NO = ((G * kTermsP + 15) / 16) * 16;  // N of the O MMA (rows of a Ps tile)
   static constexpr int kTiles = G <= 8 ? 4 : 2;             // tiles per item
   static constexpr int kChunk = kTiles * kTile;             // Top-K entries per item
-  // 16 warps (10 loaders) for G <= 8, 12 warps (6 loaders) for G = 16: whole
-  // multiples of 4 warps, so the four 16K-register sub-partitions of the SM
-  // are evenly loaded
-  static constexpr int kMaxLoaders = G <= 8 ? 10 : 6;
   static constexpr int kBufCols = (kTiles * NS + NO + 31) / 32 * 32;  // S tiles + O, per TMEM buffer
   static constexpr int kTmemCols = pow2_at_least(kTmemBufs * kBufCols);
   static constexpr int kQsBytes = NS * 128;
+  static_assert(kTiles * NS == 64 && (NO == 16 || NO == 32 || NO == 64), "TMEM load widths");
   static constexpr int kPsBytes = kTiles * NO * 128;
   // shared memory layout (offsets from a 1024-byte aligned base); every
   // region starts on a 128-byte boundary, the MMA operands on 1024
-  static constexpr int kQs = 0;                                       // [kMeta][NS][128]
-  static constexpr int kPs = kQs + kMeta * kQsBytes;                  // [2][kTiles][NO][128]
-  static constexpr int kRowTab = kPs + 2 * kPsBytes;                  // int32 [kMeta][kChunk] K/V rows
-  static constexpr int kValid = kRowTab + kMeta * kChunk * 4;         // uint8 [kMeta][kChunk]
-  static constexpr int kQinv = align128(kValid + kMeta * kChunk);     // float [kMeta][G]
-  static constexpr int kGate = align128(kQinv + kMeta * G * 4);      // bf16 [kMeta][G][128]
-  static constexpr int kRedMax = align128(kGate + kMeta * G * kHeadDim * 2);  // float [2][4][G]
-  static constexpr int kRedSum = align128(kRedMax + 2 * 4 * G * 4);   // float [2][4][G]
+  static constexpr int kQs = 0;                                        // [kMeta][NS][128]
+  static constexpr int kPs = kQs + kMeta * kQsBytes;                   // [2][kTiles][NO][128]
+  static constexpr int kRowTab = kPs + 2 * kPsBytes;                   // int32 [kMeta][kChunk] token slots
+  static constexpr int kQinv = kRowTab + kMeta * kChunk * 4;           // float [kMeta][G]
+  static constexpr int kRedMax = align128(kQinv + kMeta * G * 4);      // float [2][4][G]
+  static constexpr int kRedSum = align128(kRedMax + 2 * 4 * G * 4);    // float [2][4][G]
   static constexpr int kBars = align128(kRedSum + 2 * 4 * G * 4);
   static constexpr int kMaxSlots = 16;
   static constexpr int kNumBars = 2 * kMaxSlots + 2 * kMeta + 3 * kTmemBufs + 2;
-  static constexpr int kMisc = kBars + kNumBars * 8;                  // tmem address, abort flag
+  static constexpr int kMisc = kBars + kNumBars * 8;                   // tmem address, abort flag
   static constexpr int kSlotBase = ((kMisc + 16 + 1023) / 1024) * 1024;
   static constexpr int kSlots0 = (kSmemLimit - 1024 - kSlotBase) / kTileBytes;
-  static constexpr int kSlots = kSlots0 > kMaxLoaders ? kMaxLoaders : kSlots0;
-  // warp roles: decoder, one loader warp per ring slot (loader L refills slot
-  // L only, so every slot is refilled in order by one warp and no parity wait
-  // can be two phases off), the MMA warp, four softmax / epilogue warps
-  static constexpr int kLoaders = kSlots;                   // warps 1 .. kLoaders
-  static constexpr int kMmaWarp = 1 + kLoaders;
-  static constexpr int kSoftmax0 = kMmaWarp + 1;
-  static constexpr int kThreads = 32 * (kSoftmax0 + 4);
-  // registers per thread: each SM sub-partition has 16K registers and holds
-  // a quarter of the CTA's warps
-  static constexpr int kMaxRegs = (16384 / (((kThreads / 32 + 3) / 4) * 32)) / 8 * 8;
+  static constexpr int kSlots = kSlots0 > kMaxSlots ? kMaxSlots : kSlots0;
   static constexpr int kSmemAlloc = kSlotBase + kSlots * kTileBytes + 1024;
   static constexpr uint32_t kIdescS = idesc_e4m3(128, NS, false, false);
   static constexpr uint32_t kIdescO = idesc_e4m3(128, NO, true, false);
   static_assert(kSlots >= 2 * kTiles, "ring must hold a K and a V chunk");
-  static_assert(kSlots <= kMaxSlots, "barrier array size");
   static_assert(kSmemAlloc <= kSmemLimit, "shared memory budget");
   static_assert(kTmemCols <= 512, "TMEM budget");
   static_assert(kQs % 1024 == 0 && kPs % 1024 == 0 && kSlotBase % 1024 == 0 && kQsBytes % 1024 == 0 &&
                     (NO * 128) % 1024 == 0,
                 "MMA operands must start on 1024-byte swizzle atoms");
-  static_assert(kRowTab % 16 == 0 && kBars % 8 == 0 && kMisc % 8 == 0, "alignment of the small arrays");
+  static_assert(kRowTab % 128 == 0 && kBars % 8 == 0 && kMisc % 8 == 0, "alignment of the small arrays");
 };
 
 struct Item {
@@ -148,14 +144,33 @@ __device__ __forceinline__ int item_tiles(const DecodeParams& p, int chunk, int 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
-// Arrive on `bar` once every cp.async this thread issued so far has landed.
-__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
 }
-// Start moving the 128-byte line at `ptr` from HBM into L2 (no data returns
-// to the SM, so it occupies no shared memory and no load slot).
-__device__ __forceinline__ void prefetch_l2(const void* ptr) {
-  asm volatile("prefetch.global.L2 [%0];\n" ::"l"(ptr));
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// `bytes` (a multiple of 16, both addresses 16-byte aligned) from global to
+// shared memory through the TMA engine; completes `bytes` on `bar`.
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// Four 128-byte rows (row coordinates r0..r3 of a 2-D [rows, 128] byte tensor)
+// into 512 contiguous bytes of shared memory, 128-byte swizzled by address;
+// a row outside the tensor reads zeros. Completes 512 bytes on `bar`.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int r0, int r1,
+                                            int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
@@ -219,61 +234,11 @@ __device__ __forceinline__ float combine_p(const float* v) {
   return v[0] + v[1] * 0.0625f + v[2] * 0.00390625f + v[3] * 0.00048828125f;
 }
 
-// First-stage loads of one item for the decoder, all independent of each
-// other: the request id, the row's valid count and the Top-K indices (lane
-// owns entries lane*4..+3 of every tile). Columns past the selection read -1;
-// the count and the request id are applied when the item is finished.
-template <int kTiles>
-struct IndexStage {
-  int tok[kTiles][4];
-  int req;    // t2r[row] (unchecked)
-  int limit;  // min(topk, count)
-};
-
-template <int kTiles>
-__device__ __forceinline__ void load_index_stage(const DecodeParams& p, int item, int chunk_tokens, int lane,
-                                                 IndexStage<kTiles>& st) {
-  const Item w = item_of(p, item);
-  const int c0 = w.chunk * chunk_tokens;
-  st.req = p.t2r ? __ldg(p.t2r + w.row) : w.row;
-  st.limit = p.counts ? __ldg(p.counts + w.row)
-                      : (p.count_column ? __ldg(p.indices + (int64_t)w.row * p.indices_stride + p.topk) : p.topk);
-  const int32_t* idx_row = p.indices + (int64_t)w.row * p.indices_stride;
-#pragma unroll
-  for (int j = 0; j < kTiles; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int col = c0 + j * kTile + lane * 4 + e;
-      st.tok[j][e] = col < p.topk ? __ldg(idx_row + col) : -1;
-    }
-}
-
-// Applies the row rules of token_slot to a loaded stage: the request id must
-// index the block table and the column must lie below the row's count.
-template <int kTiles>
-__device__ __forceinline__ void mask_index_stage(const DecodeParams& p, int item, int chunk_tokens, int lane,
-                                                 IndexStage<kTiles>& st) {
-  const Item w = item_of(p, item);
-  const int c0 = w.chunk * chunk_tokens;
-  const bool req_ok = st.req >= 0 && st.req < p.num_reqs;
-  const int limit = min(p.topk, max(st.limit, 0));
-#pragma unroll
-  for (int j = 0; j < kTiles; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int col = c0 + j * kTile + lane * 4 + e;
-      if (!req_ok || col >= limit) st.tok[j][e] = -1;
-    }
-  if (!req_ok) st.req = 0;
-}
-
 template <int G>
-__global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs)
-    qsa_decode_tc_kernel(const __grid_constant__ DecodeParams p, int num_items) {
+__global__ void __launch_bounds__(kThreads, 1)
+    qsa_decode_tc_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
+                         const __grid_constant__ CUtensorMap tmap_v, int num_items) {
   using C = Cfg<G>;
-  constexpr int kLoaders = C::kLoaders;
-  constexpr int kMmaWarp = C::kMmaWarp;
-  constexpr int kSoftmax0 = C::kSoftmax0;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
   const uint32_t base_s = (raw_s + 1023u) & ~1023u;
@@ -284,7 +249,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
   const int lane = tid & 31;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBars);
-  uint64_t* kv_full = bars;                        // [kSlots] loader -> MMA
+  uint64_t* kv_full = bars;                        // [kSlots] loader TMA -> MMA
   uint64_t* kv_empty = bars + C::kMaxSlots;        // [kSlots] MMA commit -> loader
   uint64_t* meta_full = bars + 2 * C::kMaxSlots;   // [kMeta] decoder -> loaders, MMA, softmax
   uint64_t* meta_empty = meta_full + kMeta;        // [kMeta] loaders + MMA commit + softmax -> decoder
@@ -297,12 +262,15 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
   float* qinv = reinterpret_cast<float*>(smem + C::kQinv);
   float* red_max = reinterpret_cast<float*>(smem + C::kRedMax);
   float* red_sum = reinterpret_cast<float*>(smem + C::kRedSum);
-  uint8_t* valid = smem + C::kValid;
   int32_t* rowtab = reinterpret_cast<int32_t*>(smem + C::kRowTab);
+
+  // items of this CTA: blockIdx.x + k * gridDim.x for k < n_my (grid <= items)
+  const int n_my = (num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  auto item_at = [&](int k) { return (int)blockIdx.x + k * (int)gridDim.x; };
 
   if (tid == 0) {
     for (int i = 0; i < C::kSlots; ++i) {
-      mbar_init(kv_full + i, 1);
+      mbar_init(kv_full + i, 1);  // the loader's expect_tx arrival; the gathers complete the bytes
       mbar_init(kv_empty + i, 1);
     }
     for (int m = 0; m < kMeta; ++m) {
@@ -330,85 +298,24 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
 
   if (warp == kDecoderWarp) {
     // =============================== decoder ================================
-    // Software pipeline, two items deep: while item i is finished, the block
-    // table and query loads of item i+1 and the index loads of item i+2 are
-    // in flight, so one memory round trip per item overlaps everything else.
-    const int stride = gridDim.x;
-    IndexStage<C::kTiles> st_a;  // item i+2: indices, request id, count (in flight)
-    IndexStage<C::kTiles> st_b;  // item i+1: masked indices
-    int phys_b[C::kTiles][4];    // block-table entries of item i+1 (in flight), -1 = masked
-    uint2 q_b[G];                // query of item i+1 (in flight)
-    uint2 gate_b[G];             // gate of item i+1 (in flight)
-    auto issue_rest = [&](int item) {  // block-table + query loads of `item`, from st_b
-      const Item w = item_of(p, item);
-      const int32_t* bt_row = p.btable + (int64_t)st_b.req * p.btable_stride;
+    auto load_q = [&](int k, uint2 (&q)[G]) {
+      if (k < n_my) {
+        const Item w = item_of(p, item_at(k));
 #pragma unroll
-      for (int j = 0; j < C::kTiles; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = st_b.tok[j][e];
-          const int lp = p.page_shift >= 0 ? (t >> p.page_shift) : t / p.page_size;
-          const bool ok = t >= 0 && lp < p.pages_per_req;
-          phys_b[j][e] = ok ? __ldg(bt_row + lp) : -1;
-        }
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const int64_t off = ((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim + lane * 4;
-        q_b[h] = *reinterpret_cast<const uint2*>(p.q + off);
-        gate_b[h] = *reinterpret_cast<const uint2*>(p.gate + off);
+        for (int h = 0; h < G; ++h)
+          q[h] = *reinterpret_cast<const uint2*>(p.q + ((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim +
+                                                 lane * 4);
       }
     };
-    const int item0 = blockIdx.x;
-    if (item0 < num_items) {
-      load_index_stage<C::kTiles>(p, item0, C::kChunk, lane, st_b);
-      mask_index_stage<C::kTiles>(p, item0, C::kChunk, lane, st_b);
-      issue_rest(item0);
-      if (item0 + stride < num_items) load_index_stage<C::kTiles>(p, item0 + stride, C::kChunk, lane, st_a);
-    }
-    for (int it = 0, item = item0; item < num_items; ++it, item += stride) {
-      const Item w = item_of(p, item);
-      const int m = it % kMeta;
-      const int um = it / kMeta;
-
-      // results of item i (loads issued one iteration ago)
-      int coord[C::kTiles][4];
+    uint2 q_n[G];
+    load_q(0, q_n);
+    for (int k = 0; k < n_my; ++k) {
+      const Item w = item_of(p, item_at(k));
+      const int m = k % kMeta;
       uint2 q_c[G];
 #pragma unroll
-      for (int j = 0; j < C::kTiles; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = st_b.tok[j][e];
-          const int po = p.page_shift >= 0 ? (t & ((1 << p.page_shift) - 1)) : t % p.page_size;
-          const int64_t phys = phys_b[j][e];
-          coord[j][e] = (t >= 0 && phys >= 0 && phys < p.num_pages)
-                            ? (int)((phys * p.page_size + po) * p.num_kv_heads + w.g)
-                            : -1;
-        }
-      uint2 gate_c[G];
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        q_c[h] = q_b[h];
-        gate_c[h] = gate_b[h];
-      }
-      // pull every selected K and V row of item i towards L2 now: the loaders
-      // copy them into shared memory an item or more later, and by then the
-      // copies hit L2, so the ring never has to cover a full HBM round trip
-#pragma unroll
-      for (int j = 0; j < C::kTiles; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (coord[j][e] >= 0) {
-            prefetch_l2(p.k + (int64_t)coord[j][e] * kHeadDim);
-            prefetch_l2(p.v + (int64_t)coord[j][e] * kHeadDim);
-          }
-      // launch the loads of items i+1 and i+2
-      if (item + stride < num_items) {
-        st_b = st_a;
-        mask_index_stage<C::kTiles>(p, item + stride, C::kChunk, lane, st_b);
-        issue_rest(item + stride);
-        if (item + 2 * stride < num_items)
-          load_index_stage<C::kTiles>(p, item + 2 * stride, C::kChunk, lane, st_a);
-      }
+      for (int h = 0; h < G; ++h) q_c[h] = q_n[h];
+      load_q(k + 1, q_n);
 
       // query heads -> FP8 terms (lane owns dims 4*lane .. 4*lane+3)
       uint32_t qpk[G][kTermsQ];
@@ -435,11 +342,20 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
         qsc[h] = __uint_as_float((uint32_t)(127 - e) << 23) * p.score_scale_log2;
       }
 
-      // metadata slot m is free once item it-kMeta is fully consumed
+      // metadata slot m is free once item k-kMeta is fully consumed
+      const int um = k / kMeta;
       if (um > 0 &&
           !__all_sync(0xffffffffu, wait_or_abort(meta_empty + m, (uint32_t)((um - 1) & 1), abort_flag))) {
         failed = true;
         break;
+      }
+      // the item's chunk of the row map -> row table of slot m (completes on
+      // meta_full together with the arrival below)
+      if (lane == 0) {
+        mbar_expect_tx(meta_full + m, C::kChunk * 4);
+        bulk_copy_g2s(smem_u32(rowtab + m * C::kChunk),
+                      p.rowmap + (int64_t)w.row * p.rowmap_stride + (int64_t)w.chunk * C::kChunk, C::kChunk * 4,
+                      meta_full + m);
       }
       uint8_t* qs = smem + C::kQs + m * C::kQsBytes;
 #pragma unroll
@@ -448,186 +364,178 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
         for (int j = 0; j < kTermsQ; ++j)
           *reinterpret_cast<uint32_t*>(qs + sw128_offset(h * kTermsQ + j, lane * 4)) = qpk[h][j];
         if (lane == h) qinv[m * G + h] = qsc[h];
-        *reinterpret_cast<uint2*>(smem + C::kGate + ((m * G + h) * kHeadDim + lane * 4) * 2) = gate_c[h];
       }
       for (int r = G * kTermsQ; r < C::NS; ++r)  // zero padding rows of Qs
         *reinterpret_cast<uint32_t*>(qs + r * 128 + lane * 4) = 0u;
-#pragma unroll
-      for (int j = 0; j < C::kTiles; ++j) {
-        *reinterpret_cast<int4*>(rowtab + m * C::kChunk + j * kTile + lane * 4) =
-            make_int4(coord[j][0], coord[j][1], coord[j][2], coord[j][3]);
-        const uint32_t vb = (coord[j][0] >= 0 ? 1u : 0u) | (coord[j][1] >= 0 ? 0x100u : 0u) |
-                            (coord[j][2] >= 0 ? 0x10000u : 0u) | (coord[j][3] >= 0 ? 0x1000000u : 0u);
-        *reinterpret_cast<uint32_t*>(valid + m * C::kChunk + j * kTile + lane * 4) = vb;
-      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(meta_full + m);
     }
+    // drain: the last row-map copies have landed before the warp leaves
+    for (int k = max(0, n_my - kMeta); k < n_my; ++k)
+      if (!mbar_wait_bounded(meta_full + k % kMeta, (uint32_t)((k / kMeta) & 1), kWaitLimitNs)) failed = true;
   } else if (warp <= kLoaders) {
     // =============================== loaders ================================
-    // Loader warp 1+L owns ring slot L: it copies every ring position p with
-    // p % kSlots == L, in order. An item's positions are its K tiles, then its
-    // V tiles. The 128 rows of a tile go through registers into the swizzled
-    // slot, then one fence + arrive publishes the tile.
+    // The ring sequence is K(0), K(1), V(0), K(2), V(1), ..., V(n_my-1): the
+    // MMA warp's order. Position pos lands in slot pos % kSlots; loader L
+    // fills the positions of the slots s with s % kLoaders == L, in order.
     const int L = warp - 1;
-    int pos0 = 0;  // ring position of the first tile of the current item
-    int use = 0;   // fills of slot L so far
-    for (int it = 0, item = blockIdx.x; item < num_items; ++it, item += gridDim.x) {
-      const Item w = item_of(p, item);
-      const int m = it % kMeta;
-      const int ntiles = item_tiles(p, w.chunk, C::kChunk);
-      if (!__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((it / kMeta) & 1), abort_flag))) {
-        failed = true;
-        break;
+    if (lane == 0) {
+      prefetch_tmap(&tmap_k);
+      prefetch_tmap(&tmap_v);
+    }
+    int pos = 0;
+    auto load_tiles = [&](int m, int g, int ntiles, const CUtensorMap* map) -> bool {
+      const int32_t* tab = rowtab + m * C::kChunk;
+      for (int j = 0; j < ntiles; ++j, ++pos) {
+        const int s = pos % C::kSlots;
+        if (s % kLoaders != L) continue;
+        const int fill = pos / C::kSlots;
+        if (fill > 0 &&
+            !__all_sync(0xffffffffu, wait_or_abort(kv_empty + s, (uint32_t)((fill - 1) & 1), abort_flag)))
+          return false;
+        const int4 t = *reinterpret_cast<const int4*>(tab + j * kTile + lane * 4);
+        const int hkv = p.num_kv_heads;
+        if (lane == 0) mbar_arrive_expect_tx(kv_full + s, kTileBytes);
+        __syncwarp();
+        tma_gather4(base_s + C::kSlotBase + (uint32_t)s * kTileBytes + (uint32_t)lane * 512u, map, kv_full + s,
+                    t.x >= 0 ? t.x * hkv + g : -1, t.y >= 0 ? t.y * hkv + g : -1, t.z >= 0 ? t.z * hkv + g : -1,
+                    t.w >= 0 ? t.w * hkv + g : -1);
       }
-      for (int pos = pos0 + (L - pos0 % C::kSlots + C::kSlots) % C::kSlots; pos < pos0 + 2 * ntiles;
-           pos += C::kSlots, ++use) {
-        const int s = pos - pos0;
-        const bool is_v = s >= ntiles;
-        const int j = is_v ? s - ntiles : s;
-        const uint8_t* src_base = is_v ? p.v : p.k;
-        const int32_t* tab = rowtab + m * C::kChunk + j * kTile;
-        if (use > 0 &&
-            !__all_sync(0xffffffffu, wait_or_abort(kv_empty + L, (uint32_t)((use - 1) & 1), abort_flag))) {
+      return true;
+    };
+    int prev_tiles = 0, prev_g = 0;
+    for (int k = 0; k <= n_my && !failed; ++k) {
+      if (k < n_my) {
+        const int m = k % kMeta;
+        if (!__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag))) {
           failed = true;
           break;
         }
-        uint8_t* dst = smem + C::kSlotBase + L * kTileBytes;
-        // two batches of 16 warp loads; a warp load covers 4 whole 128-byte
-        // rows (8 lanes per row)
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint4 buf[kTile / 8];
-#pragma unroll
-          for (int i = 0; i < kTile / 8; ++i) {
-            const int r = (half * (kTile / 8) + i) * 4 + (lane >> 3);
-            const int rc = tab[r];
-            buf[i] = rc >= 0 ? __ldcs(reinterpret_cast<const uint4*>(src_base + (int64_t)rc * kHeadDim +
-                                                                    (lane & 7) * 16))
-                             : make_uint4(0u, 0u, 0u, 0u);
-          }
-#pragma unroll
-          for (int i = 0; i < kTile / 8; ++i) {
-            const int r = (half * (kTile / 8) + i) * 4 + (lane >> 3);
-            *reinterpret_cast<uint4*>(dst + sw128_offset(r, (lane & 7) * 16)) = buf[i];
-          }
+        const Item w = item_of(p, item_at(k));
+        if (!load_tiles(m, w.g, item_tiles(p, w.chunk, C::kChunk), &tmap_k)) {
+          failed = true;
+          break;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(kv_full + L);
       }
-      if (failed) break;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(meta_empty + m);  // this warp is done with the row table
-      pos0 += 2 * ntiles;
+      if (k >= 1) {
+        const int m1 = (k - 1) % kMeta;
+        if (!load_tiles(m1, prev_g, prev_tiles, &tmap_v)) {
+          failed = true;
+          break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(meta_empty + m1);  // this warp is done with item k-1's row table
+      }
+      if (k < n_my) {
+        const Item w = item_of(p, item_at(k));
+        prev_tiles = item_tiles(p, w.chunk, C::kChunk);
+        prev_g = w.g;
+      }
+    }
+    // drain: the gathers this warp issued have all landed before it leaves
+    // (immediate on the normal path, where the MMA warp consumed every fill)
+    for (int s = L; s < C::kSlots; s += kLoaders) {
+      const int fills = pos > s ? (pos - s + C::kSlots - 1) / C::kSlots : 0;
+      if (fills > 0 && !mbar_wait_bounded(kv_full + s, (uint32_t)((fills - 1) & 1), kWaitLimitNs)) failed = true;
     }
   } else if (warp == kMmaWarp) {
     // ================================= MMA ==================================
     if (lane == 0) {
-      int t = 0;           // ring position of the next K tile
-      int prev_v = 0;      // ring position of the previous item's first V tile
-      int prev_tiles = 0;  // tiles of the previous item
-      int prev_it = -1;
-      auto issue_o = [&](int jt, int vpos, int ntiles) -> bool {
-        const int pb = jt & 1;
-        if (!wait_or_abort(p_full + pb, (uint32_t)((jt >> 1) & 1), abort_flag)) return false;
-        tc_fence_after();
-        const int tb = jt % kTmemBufs;
-        const uint32_t d = tmem + tb * C::kBufCols + C::kTiles * C::NS;
-        for (int j = 0; j < ntiles; ++j) {
-          const int pos = vpos + j;
-          const int slot = pos % C::kSlots;
-          if (!wait_or_abort(kv_full + slot, (uint32_t)((pos / C::kSlots) & 1), abort_flag)) return false;
-          tc_fence_after();
-          const uint32_t a0 = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes;
-          const uint32_t b0 = base_s + C::kPs + pb * C::kPsBytes + j * C::NO * 128;
-#pragma unroll
-          for (int kk = 0; kk < kTile / 32; ++kk) {
-            const uint64_t ad = smem_desc_sw128(a0 + kk * 32 * 128, kTileBytes, 1024);
-            const uint64_t bd = smem_desc_sw128(b0 + kk * 32, 16, 1024);
-            mma_f8(d, ad, bd, C::kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          mma_commit(kv_empty + slot);
-        }
-        mma_commit(o_full + tb);
-        return true;
-      };
-      for (int it = 0, item = blockIdx.x; item < num_items; ++it, item += gridDim.x) {
-        const Item w = item_of(p, item);
-        const int tb = it % kTmemBufs;
-        const int ut = it / kTmemBufs;
-        const int m = it % kMeta;
-        const int ntiles = item_tiles(p, w.chunk, C::kChunk);
-        if (ut > 0 && !wait_or_abort(tmem_empty + tb, (uint32_t)((ut - 1) & 1), abort_flag)) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
-        if (!wait_or_abort(meta_full + m, (uint32_t)((it / kMeta) & 1), abort_flag)) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t qs0 = base_s + C::kQs + m * C::kQsBytes;
-        for (int j = 0; j < ntiles; ++j) {
-          const int slot = t % C::kSlots;
-          if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
+      int t = 0;  // ring position of the next tile
+      for (int k = 0; k <= n_my && !failed; ++k) {
+        if (k < n_my) {
+          // S(k) = K tiles of item k . Qs^T
+          const Item w = item_of(p, item_at(k));
+          const int tb = k % kTmemBufs;
+          const int ut = k / kTmemBufs;
+          const int m = k % kMeta;
+          const int ntiles = item_tiles(p, w.chunk, C::kChunk);
+          if (ut > 0 && !wait_or_abort(tmem_empty + tb, (uint32_t)((ut - 1) & 1), abort_flag)) {
             failed = true;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes;
-#pragma unroll
-          for (int kk = 0; kk < kHeadDim / 32; ++kk) {
-            const uint64_t ad = smem_desc_sw128(a0 + kk * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(qs0 + kk * 32, 16, 1024);
-            mma_f8(tmem + tb * C::kBufCols + j * C::NS, ad, bd, C::kIdescS, kk > 0 ? 1u : 0u);
+          if (!wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag)) {
+            failed = true;
+            break;
           }
-          mma_commit(kv_empty + slot);
-          ++t;
+          tc_fence_after();
+          const uint32_t qs0 = base_s + C::kQs + m * C::kQsBytes;
+          for (int j = 0; j < ntiles; ++j, ++t) {
+            const int slot = t % C::kSlots;
+            if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes;
+#pragma unroll
+            for (int kk = 0; kk < kHeadDim / 32; ++kk) {
+              const uint64_t ad = smem_desc_sw128(a0 + kk * 32, 16, 1024);
+              const uint64_t bd = smem_desc_sw128(qs0 + kk * 32, 16, 1024);
+              mma_f8(tmem + tb * C::kBufCols + j * C::NS, ad, bd, C::kIdescS, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(kv_empty + slot);
+          }
+          if (failed) break;
+          mma_commit(s_full + tb);
+          mma_commit(meta_empty + m);  // Qs of slot m is read once these MMAs finish
         }
-        if (failed) break;
-        mma_commit(s_full + tb);
-        mma_commit(meta_empty + m);  // Qs of slot m is read once these MMAs finish
-        const int vpos = t;          // this item's V tiles follow its K tiles
-        t += ntiles;
-        if (prev_it >= 0 && !issue_o(prev_it, prev_v, prev_tiles)) {
-          failed = true;
-          break;
+        if (k >= 1) {
+          // O^T(k-1) += V tiles of item k-1 ^T . Ps^T
+          const int jt = k - 1;
+          const int pb = jt & 1;
+          const int tb = jt % kTmemBufs;
+          const int ntiles = item_tiles(p, item_of(p, item_at(jt)).chunk, C::kChunk);
+          if (!wait_or_abort(p_full + pb, (uint32_t)((jt >> 1) & 1), abort_flag)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + tb * C::kBufCols + C::kTiles * C::NS;
+          for (int j = 0; j < ntiles; ++j, ++t) {
+            const int slot = t % C::kSlots;
+            if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes;
+            const uint32_t b0 = base_s + C::kPs + pb * C::kPsBytes + j * C::NO * 128;
+#pragma unroll
+            for (int kk = 0; kk < kTile / 32; ++kk) {
+              const uint64_t ad = smem_desc_sw128(a0 + kk * 32 * 128, kTileBytes, 1024);
+              const uint64_t bd = smem_desc_sw128(b0 + kk * 32, 16, 1024);
+              mma_f8(d, ad, bd, C::kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(kv_empty + slot);
+          }
+          if (failed) break;
+          mma_commit(o_full + tb);
         }
-        prev_it = it;
-        prev_v = vpos;
-        prev_tiles = ntiles;
       }
-      if (!failed && prev_it >= 0 && !issue_o(prev_it, prev_v, prev_tiles)) failed = true;
     }
   } else {
     // ======================== softmax + epilogue (128 thr) ==================
-    // Software pipelined: the softmax of item i runs before the epilogue of
-    // item i-1, whose O accumulation has finished meanwhile.
+    // Software pipelined: the softmax of item k runs before the epilogue of
+    // item k-1, whose O accumulation has finished meanwhile.
     const int q4 = warp & 3;          // TMEM lane quadrant of this warp
     const int sw = warp - kSoftmax0;  // 0..3
     const int tk = q4 * 32 + lane;    // token within a tile / head dim in the epilogue
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     // state of the item whose epilogue is pending
-    int e_it = -1, e_row = 0, e_g = 0, e_chunk = 0, e_ntiles = 0;
-    float e_m[G], e_l[G], e_gate[G];
+    int e_k = -1, e_row = 0, e_g = 0, e_chunk = 0, e_ntiles = 0;
+    float e_m[G], e_l[G];
+    __nv_bfloat16 e_gate[G];
     auto epilogue = [&]() {
-      const int tb = e_it % kTmemBufs;
+      const int tb = e_k % kTmemBufs;
       if (!failed)
-        failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + tb, (uint32_t)((e_it / kTmemBufs) & 1), abort_flag));
+        failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + tb, (uint32_t)((e_k / kTmemBufs) & 1), abort_flag));
       if (failed) return;
       tc_fence_after();
       float v[C::NO];
-#pragma unroll
-      for (int cb = 0; cb < C::NO; cb += 16) {
-        float tmp[16];
-        tmem_ld16(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + cb, tmp);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 16; ++c) v[cb + c] = tmp[c];
-      }
+      tmem_ld_wait<C::NO>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS, v);
       tc_fence_before();
       mbar_arrive(tmem_empty + tb);
 #pragma unroll
@@ -636,7 +544,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
                                                          : 0.f;
         const int64_t hrow = (int64_t)e_row * p.num_q_heads + e_g * G + h;
         if (p.num_chunks == 1) {
-          p.out[hrow * kHeadDim + tk] = __float2bfloat16_rn(o * p.v_scale * (1.0f / (1.0f + expf(-e_gate[h]))));
+          const float gt = __bfloat162float(e_gate[h]);
+          p.out[hrow * kHeadDim + tk] = __float2bfloat16_rn(o * p.v_scale * (1.0f / (1.0f + expf(-gt))));
         } else {
           const int64_t pidx = hrow * p.num_chunks + e_chunk;
           p.part_o[pidx * kHeadDim + tk] = o;
@@ -644,49 +553,41 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
         }
       }
     };
-    for (int it = 0, item = blockIdx.x; item < num_items; ++it, item += gridDim.x) {
-      const Item w = item_of(p, item);
-      const int tb = it % kTmemBufs;
-      const int pb = it & 1;
-      const int m = it % kMeta;
+    for (int k = 0; k < n_my; ++k) {
+      const Item w = item_of(p, item_at(k));
+      const int tb = k % kTmemBufs;
+      const int pb = k & 1;
+      const int m = k % kMeta;
       const int ntiles = item_tiles(p, w.chunk, C::kChunk);
+      // the gate of this item, needed by its epilogue one iteration later
+      __nv_bfloat16 gate[G];
+      if (p.num_chunks == 1) {
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+          gate[h] = p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim + tk];
+      }
 
-      // meta_full publishes the decoder's validity bytes, query scales and gate;
+      // meta_full publishes the decoder's validity bytes and query scales;
       // s_full the scores. Once anything failed the group keeps walking its
       // items (the named barriers must still match) but skips tensor memory.
       if (!failed) {
-        const bool ok = wait_or_abort(meta_full + m, (uint32_t)((it / kMeta) & 1), abort_flag) &&
-                        wait_or_abort(s_full + tb, (uint32_t)((it / kTmemBufs) & 1), abort_flag);
+        const bool ok = wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag) &&
+                        wait_or_abort(s_full + tb, (uint32_t)((k / kTmemBufs) & 1), abort_flag);
         failed = !__all_sync(0xffffffffu, ok);
       }
       tc_fence_after();
-      float qi[G], gate[G];
-      const __nv_bfloat16* gsm = reinterpret_cast<const __nv_bfloat16*>(smem + C::kGate) + m * G * kHeadDim;
+      float qi[G];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        qi[h] = qinv[m * G + h];
-        gate[h] = __bfloat162float(gsm[h * kHeadDim + tk]);
-      }
+      for (int h = 0; h < G; ++h) qi[h] = qinv[m * G + h];
+      // the S tiles of a buffer are kTiles * NS = 64 consecutive columns
+      float raw[C::kTiles * C::NS];
+      if (!failed) tmem_ld_wait<C::kTiles * C::NS>(tmem + lane_base + tb * C::kBufCols, raw);
       float sc[C::kTiles][G];
 #pragma unroll
       for (int j = 0; j < C::kTiles; ++j) {
-        if (j < ntiles && !failed) {
-          float v[C::NS];
+        const bool ok = !failed && j < ntiles && rowtab[m * C::kChunk + j * kTile + tk] >= 0;
 #pragma unroll
-          for (int cb = 0; cb < C::NS; cb += 16) {
-            float tmp[16];
-            tmem_ld16(tmem + lane_base + tb * C::kBufCols + j * C::NS + cb, tmp);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 16; ++c) v[cb + c] = tmp[c];
-          }
-          const bool ok = valid[m * C::kChunk + j * kTile + tk] != 0;
-#pragma unroll
-          for (int h = 0; h < G; ++h) sc[j][h] = ok ? combine_q(v + h * kTermsQ) * qi[h] : -INFINITY;
-        } else {
-#pragma unroll
-          for (int h = 0; h < G; ++h) sc[j][h] = -INFINITY;
-        }
+        for (int h = 0; h < G; ++h) sc[j][h] = ok ? combine_q(&raw[j * C::NS + h * kTermsQ]) * qi[h] : -INFINITY;
       }
       // exact max per head over the chunk
 #pragma unroll
@@ -699,7 +600,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
         if (lane == 0) red_max[(pb * 4 + sw) * G + h] = mx;
       }
       named_bar_sync(1, 128);
-      if (sw == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // validity, scales and gate read
+      if (sw == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // row table and scales read
       float m_h[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
@@ -747,8 +648,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
       }
 
       // ---- epilogue of the previous item, then this item becomes pending ---
-      if (e_it >= 0) epilogue();
-      e_it = it;
+      if (e_k >= 0) epilogue();
+      e_k = k;
       e_row = w.row;
       e_g = w.g;
       e_chunk = w.chunk;
@@ -757,10 +658,10 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
       for (int h = 0; h < G; ++h) {
         e_m[h] = m_h[h];
         e_l[h] = l_h[h];
-        e_gate[h] = gate[h];
+        e_gate[h] = p.num_chunks == 1 ? gate[h] : __float2bfloat16_rn(0.f);
       }
     }
-    if (e_it >= 0) epilogue();
+    if (e_k >= 0) epilogue();
   }
 
   if (failed) {
@@ -775,7 +676,50 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads) __maxnreg__(Cfg<G>::kMaxRegs
   }
 }
 
+// Row map: the token slot (phys * P + t % P) of every Top-K entry, -1 when
+// masked (the bit-exact decode rule of token_slot); one thread per 4 entries.
+__global__ void qsa_rowmap_kernel(const __grid_constant__ DecodeParams p) {
+  const int quads = p.rowmap_stride / 4;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)p.rows * quads) return;
+  const int row = (int)(i / quads);
+  const int c0 = (int)(i - (int64_t)row * quads) * 4;
+  const int64_t req = row_request(p, row);
+  const int count = row_count(p, row);
+  int v[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[e] = c0 + e < p.topk ? (int)token_slot(p, row, req, count, c0 + e) : -1;
+  *reinterpret_cast<int4*>(p.rowmap + (int64_t)row * p.rowmap_stride + c0) = make_int4(v[0], v[1], v[2], v[3]);
+}
+
 // ------------------------------------------------------------------ host ----
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::atomic<void*> fn{nullptr};
+  void* f = fn.load(std::memory_order_acquire);
+  if (!f) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn.store(f, std::memory_order_release);
+  }
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+}
+
+// A cache viewed as a 2-D byte tensor [num_pages * P * Hkv rows, 128]; one box
+// is one 128-byte row (gather4 moves four of them), 128-byte swizzled.
+bool encode_rows(CUtensorMap* map, const void* base, int64_t rows) {
+  auto fn = encode_fn();
+  if (!fn || rows <= 0 || rows > 0x7fffffffll) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim};
+  const cuuint32_t box[2] = {(cuuint32_t)kHeadDim, 1u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int sm_count() {
   static std::atomic<int> counts[64] = {};
   int dev = 0;
@@ -805,8 +749,12 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
   if (p.num_pages * p.page_size * p.num_kv_heads > 0x7fffffffll) return cudaErrorInvalidValue;
+  if (!p.rowmap || p.rowmap_stride != p.num_chunks * C::kChunk) return cudaErrorInvalidValue;
+  const int64_t rows = p.num_pages * p.page_size * p.num_kv_heads;
+  CUtensorMap mk, mv;
+  if (!encode_rows(&mk, p.k, rows) || !encode_rows(&mv, p.v, rows)) return cudaErrorInvalidValue;
   const int grid = (int)(items < sm_count() ? items : sm_count());
-  qsa_decode_tc_kernel<G><<<grid, C::kThreads, C::kSmemAlloc, stream>>>(p, (int)items);
+  qsa_decode_tc_kernel<G><<<grid, kThreads, C::kSmemAlloc, stream>>>(p, mk, mv, (int)items);
   return cudaGetLastError();
 }
 
@@ -816,6 +764,14 @@ int tc_chunk_tokens(int group) { return group <= 8 ? 4 * kTile : 2 * kTile; }
 
 bool tc_supports_group(int group) {
   return group == 1 || group == 2 || group == 4 || group == 8 || group == 16;
+}
+
+cudaError_t launch_rowmap(const DecodeParams& p, cudaStream_t stream) {
+  const int64_t n = (int64_t)p.rows * (p.rowmap_stride / 4);
+  if (n <= 0) return cudaSuccess;
+  const int threads = 256;
+  qsa_rowmap_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_decode_tc(const DecodeParams& p, cudaStream_t stream) {

@@ -3,16 +3,18 @@
 //
 // Some callers cannot allocate device memory at call time: a host runtime that
 // owns a fixed device budget, a latency-critical loop that must not enter the
-// CUDA allocator, or an FFI caller with no allocator. For them the split-K
-// scratch (partial outputs and log2-sum-exp of Top-K rows longer than one
-// chunk) comes from a fixed file-scope device array instead of a
-// caller-supplied workspace. The array sits in this translation unit alone,
+// CUDA allocator, or an FFI caller with no allocator (the reference-shaped
+// launch_qsa_cuda runs here too). For them the workspace (the tensor-core
+// kernel's row map, and the partial outputs and log2-sum-exps of Top-K rows
+// longer than one chunk) comes from a fixed file-scope device array instead
+// of a caller-supplied buffer. The array sits in this translation unit alone,
 // so under CUDA's lazy module loading only callers of this entry point reserve
 // it.
 //
-// Nothing in the scratch must start at zero: every chunk of every row writes
-// its partial output and its log2-sum-exp before the combine kernel, launched
-// after it on the same stream, reads them. So no clearing pass is needed.
+// Nothing in the scratch must start at zero: the row-map kernel writes every
+// entry of the row map, and every chunk of every row writes its partial output
+// and its log2-sum-exp, before the kernels launched after them on the same
+// stream read them. So no clearing pass is needed.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -53,7 +55,7 @@ void* scratch_address(int* status) {
 }  // namespace
 
 extern "C" int qsa_b200_decode_noalloc(const qsa_b200_decode_args* args, qsa_b200_stream_t stream) {
-  // validates the arguments (no device call) and sizes the split scratch
+  // validates the arguments (no device call) and sizes the workspace
   const int64_t need = qsa_b200_workspace_bytes(args);
   if (need < 0) return (int)need;
   if (need > (int64_t)QSA_B200_NOALLOC_SCRATCH_BYTES) return QSA_B200_ERR_TOO_LARGE;

@@ -119,12 +119,18 @@ def chunk_tokens(num_q_heads, num_kv_heads) -> int:
     return 512 if num_q_heads // num_kv_heads <= 8 else 256
 
 
-def workspace_bytes(rows, num_q_heads, num_kv_heads, topk) -> int:
-    """Device workspace one call needs: the per-chunk partial results when a
-    Top-K row spans more than one chunk (0 otherwise)."""
+def workspace_bytes(rows, num_q_heads, num_kv_heads, topk, kernel="auto") -> int:
+    """Device workspace one call needs, each part 256-byte aligned: the row
+    map of the tensor-core kernel (one int32 token slot per Top-K entry,
+    rows x chunks x chunk entries), then, when a Top-K row spans more than one
+    chunk, the per-chunk partial outputs and log-sum-exps."""
+    a256 = lambda x: -(-x // 256) * 256
     c = chunk_tokens(num_q_heads, num_kv_heads)
     chunks = 1 if topk <= c else -(-topk // c)
-    if chunks == 1:
-        return 0
-    n = rows * num_q_heads * chunks
-    return -(-(n * 128 * 4) // 256) * 256 + -(-(n * 4) // 256) * 256
+    group = num_q_heads // num_kv_heads
+    tc = kernel == "tc" or (kernel == "auto" and group in (1, 2, 4, 8, 16))
+    total = a256(rows * chunks * c * 4) if (tc and rows > 0) else 0
+    if chunks > 1:
+        n = rows * num_q_heads * chunks
+        total += a256(n * 128 * 4) + a256(n * 4)
+    return total
