@@ -1,11 +1,11 @@
 // C ABI of libqsa_b200.so (declared in include/qsa_b200.h).
 //
 // Validates arguments, turns them into qsa::DecodeParams and launches the
-// decode: for the tensor-core kernel (group sizes 1/2/4/8/16) the row-map
-// kernel and then the decode kernel; otherwise the CUDA-core kernel; plus the
-// split combine when a Top-K row is longer than one chunk. Workspace layout
-// (each part 256-byte aligned): the row map (tensor-core kernel only), the
-// partial outputs and the partial log-sum-exps (split rows only). No entry
+// decode (the tensor-core kernel for group sizes 1/2/4/8/16, otherwise the
+// CUDA-core kernel), plus the split combine when a Top-K row is longer than
+// one chunk. Workspace layout (each part 256-byte aligned): the row map
+// (tensor-core kernel only), the partial outputs and the partial
+// log-sum-exps (split rows only). No entry
 // point allocates, synchronises or traps.
 #include <cuda_runtime.h>
 
@@ -216,8 +216,7 @@ int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t wo
     }
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = use_tc ? launch_rowmap(p, s) : cudaSuccess;
-  if (e == cudaSuccess) e = use_tc ? launch_decode_tc(p, s) : launch_decode_simt(p, s);
+  cudaError_t e = use_tc ? launch_decode_tc(p, s) : launch_decode_simt(p, s);
   if (e != cudaSuccess) return QSA_B200_ERR_LAUNCH;
   if (p.num_chunks > 1) {
     e = launch_combine(p, s);

@@ -48,11 +48,10 @@ __device__ __forceinline__ int row_count(const DecodeParams& p, int row) {
   return c < 0 ? 0 : (c > p.topk ? p.topk : c);
 }
 
-__device__ __forceinline__ int64_t token_slot(const DecodeParams& p, int row, int64_t req, int count, int col) {
-  if (req < 0 || col >= count) return -1;
-  const int t = __ldg(p.indices + (int64_t)row * p.indices_stride + col);
-  if (t < 0) return -1;
-  int lp, po;
+// First half of the rule for a loaded index t: its logical page lp and page
+// offset po; false when the entry is masked before the block-table lookup.
+__device__ __forceinline__ bool token_page(const DecodeParams& p, int t, int& lp, int& po) {
+  if (t < 0) return false;
   if (p.page_shift >= 0) {
     lp = t >> p.page_shift;
     po = t & ((1 << p.page_shift) - 1);
@@ -60,10 +59,21 @@ __device__ __forceinline__ int64_t token_slot(const DecodeParams& p, int row, in
     lp = t / p.page_size;
     po = t - lp * p.page_size;
   }
-  if (lp >= p.pages_per_req) return -1;
-  const int64_t phys = (int64_t)__ldg(p.btable + req * p.btable_stride + lp);
-  if (phys < 0 || phys >= p.num_pages) return -1;
-  return phys * p.page_size + po;
+  return lp < p.pages_per_req;
+}
+
+// Second half: the slot of a looked-up block-table entry, -1 when the
+// physical page is out of range.
+__device__ __forceinline__ int64_t token_slot_from(const DecodeParams& p, int64_t phys, int po) {
+  return (phys < 0 || phys >= p.num_pages) ? -1 : phys * p.page_size + po;
+}
+
+__device__ __forceinline__ int64_t token_slot(const DecodeParams& p, int row, int64_t req, int count, int col) {
+  if (req < 0 || col >= count) return -1;
+  const int t = __ldg(p.indices + (int64_t)row * p.indices_stride + col);
+  int lp, po;
+  if (!token_page(p, t, lp, po)) return -1;
+  return token_slot_from(p, (int64_t)__ldg(p.btable + req * p.btable_stride + lp), po);
 }
 
 // ---------------------------------------------------------------------------
@@ -106,6 +116,12 @@ __device__ __forceinline__ void cp_async_wait_dyn(int n) {
     case 6: cp_async_wait<6>(); break;
     default: cp_async_wait<7>(); break;
   }
+}
+
+// Orders this thread's generic-proxy global writes before later async-proxy
+// (TMA) reads of the same memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;\n" ::: "memory");
 }
 
 // Make this thread's generic-proxy shared-memory writes visible to the async

@@ -4,12 +4,16 @@
 // The index decode runs first, in its own small kernel (qsa_rowmap_kernel):
 // every Top-K entry becomes its physical token slot phys * P + t % P (or -1)
 // in a row map in the workspace, in parallel over the whole GPU. The decode
-// kernel then needs no dependent global reads of its own.
+// kernel is a programmatic dependent launch of it: its prologue (barriers,
+// TMEM, tensor maps) overlaps the row map, and only the decoder warp waits
+// for the row map (griddepcontrol.wait) before its first read of it. The
+// pipeline then needs no dependent global reads of its own.
 //
 // Work item = (Top-K row, KV head, chunk of up to kTiles*128 Top-K entries).
-// Each CTA (one per SM) walks items blockIdx.x, blockIdx.x + gridDim.x, ...
-// (its k-th item is blockIdx.x + k * gridDim.x) with four roles that overlap
-// across items:
+// Each CTA (one per SM) takes items blockIdx.x, blockIdx.x + gridDim.x, ...
+// (its k-th item is blockIdx.x + k * gridDim.x, k < n_my); the item id
+// travels with the item's metadata slot, and an id of -1 after the last item
+// ends the loaders' and the MMA warp's loops. Four roles overlap across items:
 //
 //   decoder (warp 0)   for a kMeta-deep metadata ring: one TMA bulk copy brings
 //                      the item's chunk of the row map into the slot's row
@@ -28,11 +32,14 @@
 //   MMA warp           one thread issues S = K_tile . Qs^T into TMEM for every
 //                      K tile of item k, then O^T += V_tile^T . Ps^T for item
 //                      k-1 (its probabilities are ready by then);
-//   4 softmax warps    softmax over the chunk's scores (exact max and sum),
-//                      probabilities as FP8 terms of p*256 (operand Ps); then
-//                      the epilogue of the previous item (its O is complete
-//                      by then): recombine, normalise, v_scale, sigmoid gate,
-//                      bf16 store (or a partial for the split combine).
+//   softmax warps      one per TMEM lane quadrant (a second set, if
+//                      configured, splits the score tiles and epilogue heads
+//                      with the first): softmax over the chunk's scores (exact
+//                      max and sum), probabilities as FP8 terms of p*256
+//                      (operand Ps); then the epilogue of the previous item
+//                      (its O is complete by then): recombine, normalise,
+//                      v_scale, sigmoid gate, bf16 store (or a partial for the
+//                      split combine).
 //
 // Every selected 128-byte K/V row is read from HBM once and shared by the G
 // query heads. Q and P keep their precision through a split into E4M3 terms:
@@ -66,10 +73,14 @@ constexpr int kTmemBufs = 3;                  // TMEM accumulator buffers (items
 constexpr int kDecoderWarp = 0;
 constexpr int kLoaders = 6;                   // loader warps 1 .. kLoaders
 constexpr int kMmaWarp = 1 + kLoaders;
-constexpr int kSoftmax0 = kMmaWarp + 1;       // 4 softmax / epilogue warps
+constexpr int kSoftmax0 = kMmaWarp + 1;       // softmax / epilogue warps
+constexpr int kSoftmaxWarps = 4;              // 4 or 8: one or two per TMEM lane quadrant
+constexpr int kSoftmaxSets = kSoftmaxWarps / 4;
 // 12 warps, one CTA per SM: up to 168 registers per thread (each SM
 // sub-partition has 16K registers and holds a quarter of the warps)
-constexpr int kThreads = 32 * (kSoftmax0 + 4);
+constexpr int kThreads = 32 * (kSoftmax0 + kSoftmaxWarps);
+static_assert(kSoftmaxWarps == 4 || kSoftmaxWarps == 8, "softmax warp count");
+static_assert(kSoftmax0 % 4 == 0, "softmax warps must cover the four TMEM lane quadrants in order");
 constexpr int kSmemLimit = 232448;            // 227 KiB opt-in per CTA
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr int kErrTimeout = 1;
@@ -93,6 +104,9 @@ struct Cfg {
   static constexpr int kTmemCols = pow2_at_least(kTmemBufs * kBufCols);
   static constexpr int kQsBytes = NS * 128;
   static_assert(kTiles * NS == 64 && (NO == 16 || NO == 32 || NO == 64), "TMEM load widths");
+  static constexpr int kHalfTiles = kTiles / kSoftmaxSets;                    // score tiles per softmax warp
+  static constexpr int kHalfHeads = G >= kSoftmaxSets ? G / kSoftmaxSets : 1;  // epilogue heads per softmax warp
+  static constexpr int NOH = NO > 16 ? NO / kSoftmaxSets : 16;                 // O columns one softmax warp loads
   static constexpr int kPsBytes = kTiles * NO * 128;
   // shared memory layout (offsets from a 1024-byte aligned base); every
   // region starts on a 128-byte boundary, the MMA operands on 1024
@@ -100,13 +114,15 @@ struct Cfg {
   static constexpr int kPs = kQs + kMeta * kQsBytes;                   // [2][kTiles][NO][128]
   static constexpr int kRowTab = kPs + 2 * kPsBytes;                   // int32 [kMeta][kChunk] token slots
   static constexpr int kQinv = kRowTab + kMeta * kChunk * 4;           // float [kMeta][G]
-  static constexpr int kRedMax = align128(kQinv + kMeta * G * 4);      // float [2][4][G]
-  static constexpr int kRedSum = align128(kRedMax + 2 * 4 * G * 4);    // float [2][4][G]
-  static constexpr int kBars = align128(kRedSum + 2 * 4 * G * 4);
+  static constexpr int kRedMax = align128(kQinv + kMeta * G * 4);      // float [2][8][G]
+  static constexpr int kRedSum = align128(kRedMax + 2 * kSoftmaxWarps * G * 4);  // float [2][8][G]
+  static constexpr int kBars = align128(kRedSum + 2 * kSoftmaxWarps * G * 4);
   static constexpr int kMaxSlots = 16;
   static constexpr int kNumBars = 2 * kMaxSlots + 2 * kMeta + 3 * kTmemBufs + 2;
-  static constexpr int kMisc = kBars + kNumBars * 8;                   // tmem address, abort flag
-  static constexpr int kSlotBase = ((kMisc + 16 + 1023) / 1024) * 1024;
+  // tmem address (+0), abort flag (+8), item ids of the metadata slots
+  // (+16, kMeta ints)
+  static constexpr int kMisc = kBars + kNumBars * 8;
+  static constexpr int kSlotBase = ((kMisc + 48 + 1023) / 1024) * 1024;
   static constexpr int kSlots0 = (kSmemLimit - 1024 - kSlotBase) / kTileBytes;
   static constexpr int kSlots = kSlots0 > kMaxSlots ? kMaxSlots : kSlots0;
   static constexpr int kSmemAlloc = kSlotBase + kSlots * kTileBytes + 1024;
@@ -118,7 +134,7 @@ struct Cfg {
   static_assert(kQs % 1024 == 0 && kPs % 1024 == 0 && kSlotBase % 1024 == 0 && kQsBytes % 1024 == 0 &&
                     (NO * 128) % 1024 == 0,
                 "MMA operands must start on 1024-byte swizzle atoms");
-  static_assert(kRowTab % 128 == 0 && kBars % 8 == 0 && kMisc % 8 == 0, "alignment of the small arrays");
+  static_assert(kRowTab % 128 == 0 && kBars % 8 == 0 && kMisc % 8 == 0 && kMeta <= 8, "alignment of the small arrays");
 };
 
 struct Item {
@@ -186,7 +202,10 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
     if (*abort_flag) return false;
     uint64_t t1;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-    if (t1 - t0 > kWaitLimitNs) return false;
+    if (t1 - t0 > kWaitLimitNs) {
+      *abort_flag = 1;  // the other roles leave their loops at their next wait
+      return false;
+    }
   }
 }
 
@@ -259,14 +278,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = tmem_empty + kTmemBufs;       // [2] softmax -> MMA (Ps double buffer)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMisc + 8);
-  float* qinv = reinterpret_cast<float*>(smem + C::kQinv);
-  float* red_max = reinterpret_cast<float*>(smem + C::kRedMax);
-  float* red_sum = reinterpret_cast<float*>(smem + C::kRedSum);
-  int32_t* rowtab = reinterpret_cast<int32_t*>(smem + C::kRowTab);
+  volatile int* item_ids = reinterpret_cast<volatile int*>(smem + C::kMisc + 16);  // [kMeta]
 
   // items of this CTA: blockIdx.x + k * gridDim.x for k < n_my (grid <= items)
   const int n_my = (num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   auto item_at = [&](int k) { return (int)blockIdx.x + k * (int)gridDim.x; };
+  float* qinv = reinterpret_cast<float*>(smem + C::kQinv);
+  float* red_max = reinterpret_cast<float*>(smem + C::kRedMax);
+  float* red_sum = reinterpret_cast<float*>(smem + C::kRedSum);
+  int32_t* rowtab = reinterpret_cast<int32_t*>(smem + C::kRowTab);
 
   if (tid == 0) {
     for (int i = 0; i < C::kSlots; ++i) {
@@ -280,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < kTmemBufs; ++b) {
       mbar_init(s_full + b, 1);
       mbar_init(o_full + b, 1);
-      mbar_init(tmem_empty + b, 128);
+      mbar_init(tmem_empty + b, 32 * kSoftmaxWarps);
     }
     for (int b = 0; b < 2; ++b) mbar_init(p_full + b, 1);
     *abort_flag = 0;
@@ -291,6 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
     tc_fence_before();
   }
+  // every warp reaches the CTA barriers converged: a warp that arrives in
+  // pieces would be counted more than once and release the barrier early
+  __syncwarp();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -298,9 +321,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kDecoderWarp) {
     // =============================== decoder ================================
-    auto load_q = [&](int k, uint2 (&q)[G]) {
-      if (k < n_my) {
-        const Item w = item_of(p, item_at(k));
+    auto load_q = [&](int item, uint2 (&q)[G]) {
+      if (item < num_items) {
+        const Item w = item_of(p, item);
 #pragma unroll
         for (int h = 0; h < G; ++h)
           q[h] = *reinterpret_cast<const uint2*>(p.q + ((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim +
@@ -308,14 +331,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     uint2 q_n[G];
-    load_q(0, q_n);
-    for (int k = 0; k < n_my; ++k) {
-      const Item w = item_of(p, item_at(k));
+    load_q(item_at(0), q_n);
+    // the row map is written by the preceding kernel of this programmatic
+    // dependent launch
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    int k = 0;
+    for (;; ++k) {
+      const bool last = k == n_my;
+      const int item = item_at(k);
       const int m = k % kMeta;
       uint2 q_c[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) q_c[h] = q_n[h];
-      load_q(k + 1, q_n);
+      if (!last) load_q(item_at(k + 1), q_n);
 
       // query heads -> FP8 terms (lane owns dims 4*lane .. 4*lane+3)
       uint32_t qpk[G][kTermsQ];
@@ -349,6 +377,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         failed = true;
         break;
       }
+      if (last) {
+        // end of work: id -1 in slot m tells every role to finish
+        if (lane == 0) {
+          item_ids[m] = -1;
+          mbar_arrive(meta_full + m);
+        }
+        break;
+      }
+      const Item w = item_of(p, item);
       // the item's chunk of the row map -> row table of slot m (completes on
       // meta_full together with the arrival below)
       if (lane == 0) {
@@ -356,6 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_copy_g2s(smem_u32(rowtab + m * C::kChunk),
                       p.rowmap + (int64_t)w.row * p.rowmap_stride + (int64_t)w.chunk * C::kChunk, C::kChunk * 4,
                       meta_full + m);
+        item_ids[m] = item;
       }
       uint8_t* qs = smem + C::kQs + m * C::kQsBytes;
 #pragma unroll
@@ -371,12 +409,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(meta_full + m);
     }
-    // drain: the last row-map copies have landed before the warp leaves
-    for (int k = max(0, n_my - kMeta); k < n_my; ++k)
-      if (!mbar_wait_bounded(meta_full + k % kMeta, (uint32_t)((k / kMeta) & 1), kWaitLimitNs)) failed = true;
+    // drain: the last row-map copies have landed before the warp leaves (the
+    // end-of-work slot k took the slot of item k - kMeta, whose copy the
+    // consumers had already waited for)
+    for (int kk = max(0, k - kMeta + 1); kk < k; ++kk)
+      if (!mbar_wait_bounded(meta_full + kk % kMeta, (uint32_t)((kk / kMeta) & 1), kWaitLimitNs)) failed = true;
   } else if (warp <= kLoaders) {
     // =============================== loaders ================================
-    // The ring sequence is K(0), K(1), V(0), K(2), V(1), ..., V(n_my-1): the
+    // The ring sequence is K(0), K(1), V(0), K(2), V(1), ..., V(last): the
     // MMA warp's order. Position pos lands in slot pos % kSlots; loader L
     // fills the positions of the slots s with s % kLoaders == L, in order.
     const int L = warp - 1;
@@ -405,20 +445,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     int prev_tiles = 0, prev_g = 0;
-    for (int k = 0; k <= n_my && !failed; ++k) {
-      if (k < n_my) {
-        const int m = k % kMeta;
-        if (!__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag))) {
-          failed = true;
-          break;
-        }
-        const Item w = item_of(p, item_at(k));
-        if (!load_tiles(m, w.g, item_tiles(p, w.chunk, C::kChunk), &tmap_k)) {
-          failed = true;
-          break;
-        }
+    bool have_prev = false;
+    for (int k = 0; !failed; ++k) {
+      const int m = k % kMeta;
+      if (!__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag))) {
+        failed = true;
+        break;
       }
-      if (k >= 1) {
+      const int item = item_ids[m];
+      const Item w = item_of(p, item >= 0 ? item : 0);
+      if (item >= 0 && !load_tiles(m, w.g, item_tiles(p, w.chunk, C::kChunk), &tmap_k)) {
+        failed = true;
+        break;
+      }
+      if (have_prev) {
         const int m1 = (k - 1) % kMeta;
         if (!load_tiles(m1, prev_g, prev_tiles, &tmap_v)) {
           failed = true;
@@ -427,11 +467,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(meta_empty + m1);  // this warp is done with item k-1's row table
       }
-      if (k < n_my) {
-        const Item w = item_of(p, item_at(k));
-        prev_tiles = item_tiles(p, w.chunk, C::kChunk);
-        prev_g = w.g;
-      }
+      if (item < 0) break;
+      prev_tiles = item_tiles(p, w.chunk, C::kChunk);
+      prev_g = w.g;
+      have_prev = true;
     }
     // drain: the gathers this warp issued have all landed before it leaves
     // (immediate on the normal path, where the MMA warp consumed every fill)
@@ -443,20 +482,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ================================= MMA ==================================
     if (lane == 0) {
       int t = 0;  // ring position of the next tile
-      for (int k = 0; k <= n_my && !failed; ++k) {
-        if (k < n_my) {
+      int prev_tiles = 0;
+      bool have_prev = false;
+      for (int k = 0; !failed; ++k) {
+        const int m = k % kMeta;
+        if (!wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag)) {
+          failed = true;
+          break;
+        }
+        const int item = item_ids[m];
+        const int ntiles = item >= 0 ? item_tiles(p, item_of(p, item).chunk, C::kChunk) : 0;
+        if (item >= 0) {
           // S(k) = K tiles of item k . Qs^T
-          const Item w = item_of(p, item_at(k));
           const int tb = k % kTmemBufs;
           const int ut = k / kTmemBufs;
-          const int m = k % kMeta;
-          const int ntiles = item_tiles(p, w.chunk, C::kChunk);
           if (ut > 0 && !wait_or_abort(tmem_empty + tb, (uint32_t)((ut - 1) & 1), abort_flag)) {
-            failed = true;
-            break;
-          }
-          tc_fence_after();
-          if (!wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag)) {
             failed = true;
             break;
           }
@@ -482,19 +522,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(s_full + tb);
           mma_commit(meta_empty + m);  // Qs of slot m is read once these MMAs finish
         }
-        if (k >= 1) {
+        if (have_prev) {
           // O^T(k-1) += V tiles of item k-1 ^T . Ps^T
           const int jt = k - 1;
           const int pb = jt & 1;
           const int tb = jt % kTmemBufs;
-          const int ntiles = item_tiles(p, item_of(p, item_at(jt)).chunk, C::kChunk);
           if (!wait_or_abort(p_full + pb, (uint32_t)((jt >> 1) & 1), abort_flag)) {
             failed = true;
             break;
           }
           tc_fence_after();
           const uint32_t d = tmem + tb * C::kBufCols + C::kTiles * C::NS;
-          for (int j = 0; j < ntiles; ++j, ++t) {
+          for (int j = 0; j < prev_tiles; ++j, ++t) {
             const int slot = t % C::kSlots;
             if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
               failed = true;
@@ -514,62 +553,79 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (failed) break;
           mma_commit(o_full + tb);
         }
+        if (item < 0) break;
+        prev_tiles = ntiles;
+        have_prev = true;
       }
     }
+    // the other 31 lanes wait here for lane 0, so that the whole warp reaches
+    // the CTA barrier below together (a barrier met by a diverged warp would
+    // let the CTA pass it before lane 0 is done)
+    __syncwarp();
   } else {
-    // ======================== softmax + epilogue (128 thr) ==================
+    // ======================== softmax + epilogue ==========================
     // Software pipelined: the softmax of item k runs before the epilogue of
-    // item k-1, whose O accumulation has finished meanwhile.
-    const int q4 = warp & 3;          // TMEM lane quadrant of this warp
-    const int sw = warp - kSoftmax0;  // 0..3
-    const int tk = q4 * 32 + lane;    // token within a tile / head dim in the epilogue
+    // item k-1, whose O accumulation has finished meanwhile. With two sets of
+    // softmax warps, warps sw and sw + 4 share a TMEM lane quadrant and `half`
+    // picks their score tiles and epilogue heads.
+    const int q4 = warp & 3;                // TMEM lane quadrant of this warp
+    const int sw = warp - kSoftmax0;        // 0 .. kSoftmaxWarps-1
+    const int half = kSoftmaxSets > 1 ? (sw >> 2) : 0;  // softmax set
+    const int tk = q4 * 32 + lane;          // token within a tile / head dim in the epilogue
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const int j0 = half * C::kHalfTiles;    // first score tile of this warp
+    const int h0 = half * C::kHalfHeads;    // first epilogue head of this warp
+    const bool has_heads = h0 < G;          // false only for the second half when G == 1
+    // O columns this warp loads: the NOH-column block holding its heads' terms
+    const int ocol0 = C::NO > C::NOH ? half * C::NOH : 0;
     // state of the item whose epilogue is pending
     int e_k = -1, e_row = 0, e_g = 0, e_chunk = 0, e_ntiles = 0;
-    float e_m[G], e_l[G];
-    __nv_bfloat16 e_gate[G];
+    float e_m[C::kHalfHeads], e_l[C::kHalfHeads];
+    __nv_bfloat16 e_gate[C::kHalfHeads];
     auto epilogue = [&]() {
       const int tb = e_k % kTmemBufs;
       if (!failed)
         failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + tb, (uint32_t)((e_k / kTmemBufs) & 1), abort_flag));
       if (failed) return;
       tc_fence_after();
-      float v[C::NO];
-      tmem_ld_wait<C::NO>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS, v);
+      float v[C::NOH];
+      tmem_ld_wait<C::NOH>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + ocol0, v);
       tc_fence_before();
       mbar_arrive(tmem_empty + tb);
+      if (!has_heads) return;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float o = (e_ntiles > 0 && e_l[h] > 0.f) ? combine_p(v + h * kTermsP) * (1.0f / 256.0f) / e_l[h]
-                                                         : 0.f;
+      for (int hh = 0; hh < C::kHalfHeads; ++hh) {
+        const int h = h0 + hh;
+        const float o = (e_ntiles > 0 && e_l[hh] > 0.f)
+                            ? combine_p(v + h * kTermsP - ocol0) * (1.0f / 256.0f) / e_l[hh]
+                            : 0.f;
         const int64_t hrow = (int64_t)e_row * p.num_q_heads + e_g * G + h;
         if (p.num_chunks == 1) {
-          const float gt = __bfloat162float(e_gate[h]);
+          const float gt = __bfloat162float(e_gate[hh]);
           p.out[hrow * kHeadDim + tk] = __float2bfloat16_rn(o * p.v_scale * (1.0f / (1.0f + expf(-gt))));
         } else {
           const int64_t pidx = hrow * p.num_chunks + e_chunk;
           p.part_o[pidx * kHeadDim + tk] = o;
-          if (tk == 0) p.part_lse[pidx] = e_l[h] > 0.f ? e_m[h] + log2f(e_l[h]) : -INFINITY;
+          if (tk == 0) p.part_lse[pidx] = e_l[hh] > 0.f ? e_m[hh] + log2f(e_l[hh]) : -INFINITY;
         }
       }
     };
     for (int k = 0; k < n_my; ++k) {
-      const Item w = item_of(p, item_at(k));
       const int tb = k % kTmemBufs;
       const int pb = k & 1;
       const int m = k % kMeta;
+      const Item w = item_of(p, item_at(k));
       const int ntiles = item_tiles(p, w.chunk, C::kChunk);
-      // the gate of this item, needed by its epilogue one iteration later
-      __nv_bfloat16 gate[G];
-      if (p.num_chunks == 1) {
+      // the gate of this warp's heads, needed by the epilogue one iteration later
+      __nv_bfloat16 gate[C::kHalfHeads];
+      if (p.num_chunks == 1 && has_heads) {
 #pragma unroll
-        for (int h = 0; h < G; ++h)
-          gate[h] = p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim + tk];
+        for (int hh = 0; hh < C::kHalfHeads; ++hh)
+          gate[hh] = p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h0 + hh) * kHeadDim + tk];
       }
-
-      // meta_full publishes the decoder's validity bytes and query scales;
-      // s_full the scores. Once anything failed the group keeps walking its
-      // items (the named barriers must still match) but skips tensor memory.
+      // meta_full publishes the row table and query scales; s_full the
+      // scores. Once anything failed the group keeps walking its items (the
+      // named barriers must still match) but skips tensor memory.
       if (!failed) {
         const bool ok = wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag) &&
                         wait_or_abort(s_full + tb, (uint32_t)((k / kTmemBufs) & 1), abort_flag);
@@ -579,73 +635,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       float qi[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) qi[h] = qinv[m * G + h];
-      // the S tiles of a buffer are kTiles * NS = 64 consecutive columns
-      float raw[C::kTiles * C::NS];
-      if (!failed) tmem_ld_wait<C::kTiles * C::NS>(tmem + lane_base + tb * C::kBufCols, raw);
-      float sc[C::kTiles][G];
+      // this warp's score tiles: kHalfTiles * NS consecutive columns
+      float raw[C::kHalfTiles * C::NS];
+      if (!failed) tmem_ld_wait<C::kHalfTiles * C::NS>(tmem + lane_base + tb * C::kBufCols + j0 * C::NS, raw);
+      float sc[C::kHalfTiles][G];
 #pragma unroll
-      for (int j = 0; j < C::kTiles; ++j) {
+      for (int jj = 0; jj < C::kHalfTiles; ++jj) {
+        const int j = j0 + jj;
         const bool ok = !failed && j < ntiles && rowtab[m * C::kChunk + j * kTile + tk] >= 0;
 #pragma unroll
-        for (int h = 0; h < G; ++h) sc[j][h] = ok ? combine_q(&raw[j * C::NS + h * kTermsQ]) * qi[h] : -INFINITY;
+        for (int h = 0; h < G; ++h) sc[jj][h] = ok ? combine_q(&raw[jj * C::NS + h * kTermsQ]) * qi[h] : -INFINITY;
       }
-      // exact max per head over the chunk
+      // exact max per head over the chunk (one partial maximum per softmax warp)
 #pragma unroll
       for (int h = 0; h < G; ++h) {
         float mx = sc[0][h];
 #pragma unroll
-        for (int j = 1; j < C::kTiles; ++j) mx = fmaxf(mx, sc[j][h]);
+        for (int jj = 1; jj < C::kHalfTiles; ++jj) mx = fmaxf(mx, sc[jj][h]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) red_max[(pb * 4 + sw) * G + h] = mx;
+        if (lane == 0) red_max[(pb * kSoftmaxWarps + sw) * G + h] = mx;
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 32 * kSoftmaxWarps);
       if (sw == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // row table and scales read
       float m_h[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float* rm = red_max + pb * 4 * G + h;
-        m_h[h] = fmaxf(fmaxf(rm[0], rm[G]), fmaxf(rm[2 * G], rm[3 * G]));
+        const float* rm = red_max + pb * kSoftmaxWarps * G + h;
+        float mx = rm[0];
+#pragma unroll
+        for (int i = 1; i < kSoftmaxWarps; ++i) mx = fmaxf(mx, rm[i * G]);
+        m_h[h] = mx;
         float sum = 0.f;
 #pragma unroll
-        for (int j = 0; j < C::kTiles; ++j) {
-          const float pr = sc[j][h] == -INFINITY ? 0.f : exp2f(sc[j][h] - m_h[h]);
-          sc[j][h] = pr;
+        for (int jj = 0; jj < C::kHalfTiles; ++jj) {
+          const float pr = sc[jj][h] == -INFINITY ? 0.f : exp2f(sc[jj][h] - mx);
+          sc[jj][h] = pr;
           sum += pr;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) red_sum[(pb * 4 + sw) * G + h] = sum;
+        if (lane == 0) red_sum[(pb * kSoftmaxWarps + sw) * G + h] = sum;
       }
       // probabilities -> FP8 terms of p*256 (row h*kTermsP+j of Ps, one byte per
       // token), two heads per conversion
       uint8_t* ps = smem + C::kPs + pb * C::kPsBytes;
 #pragma unroll
-      for (int j = 0; j < C::kTiles; ++j) {
+      for (int jj = 0; jj < C::kHalfTiles; ++jj) {
+        const int j = j0 + jj;
         if (j < ntiles) {
           uint8_t* pt = ps + j * C::NO * 128;
 #pragma unroll
           for (int h = 0; h < G; h += 2) {
             uint16_t tt[kTermsP];
-            split_p2(sc[j][h] * 256.0f, h + 1 < G ? sc[j][h + 1] * 256.0f : 0.f, tt);
+            split_p2(sc[jj][h] * 256.0f, h + 1 < G ? sc[jj][h + 1] * 256.0f : 0.f, tt);
 #pragma unroll
-            for (int jj = 0; jj < kTermsP; ++jj) {
-              pt[sw128_offset(h * kTermsP + jj, tk)] = (uint8_t)(tt[jj] & 0xffu);
-              if (h + 1 < G) pt[sw128_offset((h + 1) * kTermsP + jj, tk)] = (uint8_t)(tt[jj] >> 8);
+            for (int t = 0; t < kTermsP; ++t) {
+              pt[sw128_offset(h * kTermsP + t, tk)] = (uint8_t)(tt[t] & 0xffu);
+              if (h + 1 < G) pt[sw128_offset((h + 1) * kTermsP + t, tk)] = (uint8_t)(tt[t] >> 8);
             }
           }
           for (int r = G * kTermsP; r < C::NO; ++r) pt[sw128_offset(r, tk)] = 0;
         }
       }
       fence_proxy_async_smem();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 32 * kSoftmaxWarps);
       if (sw == 0 && lane == 0 && !failed) mbar_arrive(p_full + pb);
-      float l_h[G];
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float* rs = red_sum + pb * 4 * G + h;
-        l_h[h] = rs[0] + rs[G] + rs[2 * G] + rs[3 * G];
-      }
 
       // ---- epilogue of the previous item, then this item becomes pending ---
       if (e_k >= 0) epilogue();
@@ -655,10 +710,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       e_chunk = w.chunk;
       e_ntiles = ntiles;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        e_m[h] = m_h[h];
-        e_l[h] = l_h[h];
-        e_gate[h] = p.num_chunks == 1 ? gate[h] : __float2bfloat16_rn(0.f);
+      for (int hh = 0; hh < C::kHalfHeads; ++hh) {
+        const int h = min(h0 + hh, G - 1);
+        const float* rs = red_sum + pb * kSoftmaxWarps * G + h;
+        float l = 0.f;
+#pragma unroll
+        for (int i = 0; i < kSoftmaxWarps; ++i) l += rs[i * G];
+        e_m[hh] = m_h[h];
+        e_l[hh] = l;
+        e_gate[hh] = (p.num_chunks == 1 && has_heads) ? gate[hh] : __float2bfloat16_rn(0.f);
       }
     }
     if (e_k >= 0) epilogue();
@@ -668,6 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 1;
     report_error(p, kErrTimeout);
   }
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -677,19 +738,55 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Row map: the token slot (phys * P + t % P) of every Top-K entry, -1 when
-// masked (the bit-exact decode rule of token_slot); one thread per 4 entries.
-__global__ void qsa_rowmap_kernel(const __grid_constant__ DecodeParams p) {
+// masked (the rule of token_slot). Each thread handles kBatch quads of four
+// entries, spaced a grid apart, with all their index loads and then all
+// their block-table loads in flight together.
+constexpr int kRowmapBatch = 1;
+constexpr int kRowmapThreads = 256;
+
+__global__ void __launch_bounds__(kRowmapThreads) qsa_rowmap_kernel(const __grid_constant__ DecodeParams p) {
+  // let the decode kernel launch now; it waits for this grid before reading
+  // the map
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const int quads = p.rowmap_stride / 4;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)p.rows * quads) return;
-  const int row = (int)(i / quads);
-  const int c0 = (int)(i - (int64_t)row * quads) * 4;
-  const int64_t req = row_request(p, row);
-  const int count = row_count(p, row);
-  int v[4];
+  const int64_t total = (int64_t)p.rows * quads;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t q0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int t[kRowmapBatch][4], lim[kRowmapBatch], col0[kRowmapBatch], row[kRowmapBatch];
+  int64_t req[kRowmapBatch];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) v[e] = c0 + e < p.topk ? (int)token_slot(p, row, req, count, c0 + e) : -1;
-  *reinterpret_cast<int4*>(p.rowmap + (int64_t)row * p.rowmap_stride + c0) = make_int4(v[0], v[1], v[2], v[3]);
+  for (int b = 0; b < kRowmapBatch; ++b) {
+    const int64_t q = q0 + b * stride;
+    row[b] = -1;
+    if (q < total) {
+      row[b] = (int)(q / quads);
+      col0[b] = (int)(q - (int64_t)row[b] * quads) * 4;
+      req[b] = row_request(p, row[b]);
+      lim[b] = row_count(p, row[b]);
+      const int32_t* ip = p.indices + (int64_t)row[b] * p.indices_stride;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) t[b][e] = col0[b] + e < p.topk ? __ldg(ip + col0[b] + e) : -1;
+    }
+  }
+  int64_t ph[kRowmapBatch][4];
+  int po[kRowmapBatch][4];
+#pragma unroll
+  for (int b = 0; b < kRowmapBatch; ++b)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int lp = 0;
+      po[b][e] = 0;
+      const bool ok = row[b] >= 0 && req[b] >= 0 && col0[b] + e < lim[b] && token_page(p, t[b][e], lp, po[b][e]);
+      ph[b][e] = ok ? (int64_t)__ldg(p.btable + req[b] * p.btable_stride + lp) : -1;
+    }
+#pragma unroll
+  for (int b = 0; b < kRowmapBatch; ++b)
+    if (row[b] >= 0)
+      *reinterpret_cast<int4*>(p.rowmap + (int64_t)row[b] * p.rowmap_stride + col0[b]) =
+          make_int4((int)token_slot_from(p, ph[b][0], po[b][0]), (int)token_slot_from(p, ph[b][1], po[b][1]),
+                    (int)token_slot_from(p, ph[b][2], po[b][2]), (int)token_slot_from(p, ph[b][3], po[b][3]));
+  // the decode kernel reads the map through TMA (the async proxy)
+  fence_proxy_async_global();
 }
 
 // ------------------------------------------------------------------ host ----
@@ -754,8 +851,24 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   CUtensorMap mk, mv;
   if (!encode_rows(&mk, p.k, rows) || !encode_rows(&mv, p.v, rows)) return cudaErrorInvalidValue;
   const int grid = (int)(items < sm_count() ? items : sm_count());
-  qsa_decode_tc_kernel<G><<<grid, kThreads, C::kSmemAlloc, stream>>>(p, mk, mv, (int)items);
-  return cudaGetLastError();
+
+  // the row map, then the decode as its programmatic dependent
+  const int64_t quads = (int64_t)p.rows * (p.rowmap_stride / 4);
+  const int64_t per_block = (int64_t)kRowmapThreads * kRowmapBatch;
+  qsa_rowmap_kernel<<<(unsigned)((quads + per_block - 1) / per_block), kRowmapThreads, 0, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)kThreads);
+  cfg.dynamicSmemBytes = (size_t)C::kSmemAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, qsa_decode_tc_kernel<G>, p, mk, mv, (int)items);
 }
 
 }  // namespace
@@ -764,14 +877,6 @@ int tc_chunk_tokens(int group) { return group <= 8 ? 4 * kTile : 2 * kTile; }
 
 bool tc_supports_group(int group) {
   return group == 1 || group == 2 || group == 4 || group == 8 || group == 16;
-}
-
-cudaError_t launch_rowmap(const DecodeParams& p, cudaStream_t stream) {
-  const int64_t n = (int64_t)p.rows * (p.rowmap_stride / 4);
-  if (n <= 0) return cudaSuccess;
-  const int threads = 256;
-  qsa_rowmap_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(p);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_decode_tc(const DecodeParams& p, cudaStream_t stream) {

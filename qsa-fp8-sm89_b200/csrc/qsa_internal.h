@@ -46,10 +46,11 @@ struct DecodeParams {
   float* part_o;    // [rows, Hq, num_chunks, 128] normalised partial outputs
   float* part_lse;  // [rows, Hq, num_chunks] log2-sum-exp2 of each chunk (-inf if empty)
 
-  // Row map of the tensor-core kernel (workspace): for every Top-K entry of
-  // every row, the physical token slot phys * P + t % P, or -1 when masked;
-  // row r's entries start at rowmap + r * rowmap_stride (num_chunks *
-  // chunk_tokens entries, the tail past topk -1).
+  // Row map of the tensor-core kernel (workspace, filled by its row-map
+  // kernel): for every Top-K entry of every row, the physical token slot
+  // phys * P + t % P, or -1 when masked; row r's entries start at
+  // rowmap + r * rowmap_stride (num_chunks * chunk_tokens entries, the tail
+  // past topk -1).
   int32_t* rowmap;
   int rowmap_stride;
 
@@ -61,8 +62,6 @@ cudaError_t launch_decode_tc(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_decode_simt(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_slots(const DecodeParams& p, int64_t* slots, cudaStream_t stream);
-// Fills p.rowmap (the tensor-core kernel's index decode, run before it).
-cudaError_t launch_rowmap(const DecodeParams& p, cudaStream_t stream);
 
 // Top-K entries per work item for a GQA group size (both kernels split rows
 // the same way, so the workspace size depends only on the shape), and the
