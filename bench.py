@@ -41,10 +41,10 @@ METRIC = "µs/call + achieved HBM TB/s (vs ~8 TB/s) @256 req, TopK 512; 1/2/4/8 
 FLUSH_BYTES = 256 << 20
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch on the
-# bench workload, from the ncu capture summarised in profiles/ (None until
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch on
+# the bench workload, from the ncu capture summarised in profiles/ (None until
 # captured for the current kernel).
-NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): 276_772_096}
+NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): 278_276_864}
 
 
 def parse():
@@ -271,7 +271,12 @@ def run_ours(args):
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     out = torch.empty_like(w.q)
     kernel = args.kernel
-    launches_per_call = 1 + (1 if w.meta["topk"] > 512 else 0)
+    # tensor-core path: the row-map kernel and the decode kernel (+ the split
+    # combine for Top-K rows longer than one chunk); CUDA-core path: the decode
+    # kernel (+ combine)
+    chunk = 512 if w.meta["hq"] // w.meta["hkv"] <= 8 else 256
+    tc_path = kernel == "tc" or (kernel == "auto" and w.meta["hq"] // w.meta["hkv"] in (1, 2, 4, 8, 16))
+    launches_per_call = (2 if tc_path else 1) + (1 if w.meta["topk"] > chunk else 0)
 
     def call():
         qsa_b200.qsa_decode(*w.args(), out=out, kernel=kernel)
@@ -366,7 +371,8 @@ def run_ours(args):
             "logical_kv_tbs": total_logical / (step_ms * 1e-3) / 1e12,
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                          "frac": achieved_gbs / peak, "peak_source": peak_kind,
-                         "traffic": traffic, "kernel": f"qsa_decode_{kname}_kernel"},
+                         "traffic": traffic, "kernel": f"qsa_decode_{kname}_kernel",
+                         "timed": "whole call (row-map kernel + decode kernel), CUDA events on the launch stream"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
