@@ -3,9 +3,9 @@
 // Validates arguments, turns them into qsa::DecodeParams and launches the
 // decode (the tensor-core kernel for group sizes 1/2/4/8/16, otherwise the
 // CUDA-core kernel), plus the split combine when a Top-K row is longer than
-// one chunk. Workspace layout (each part 256-byte aligned): the row map
-// (tensor-core kernel only), the partial outputs and the partial
-// log-sum-exps (split rows only). No entry
+// one chunk. Workspace layout (each part 256-byte aligned): the row map and
+// the tile flags (tensor-core kernel only), the partial outputs and the
+// partial log-sum-exps (split rows only). No entry
 // point allocates, synchronises or traps.
 #include <cuda_runtime.h>
 
@@ -132,6 +132,7 @@ void fill_params(const qsa_b200_decode_args* a, DecodeParams* p) {
   p->part_lse = nullptr;
   p->rowmap = nullptr;
   p->rowmap_stride = p->num_chunks * p->chunk_tokens;
+  p->tile_flags = nullptr;
   p->err = nullptr;
 }
 
@@ -141,7 +142,7 @@ bool uses_tc(const qsa_b200_decode_args* a, int group) {
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-// Workspace parts: [row map][partial outputs][partial log-sum-exps].
+// Workspace parts: [row map, tile flags][partial outputs][partial log-sum-exps].
 struct WorkspaceLayout {
   int64_t rowmap_bytes, part_o_bytes, part_lse_bytes;
   int64_t total() const { return rowmap_bytes + part_o_bytes + part_lse_bytes; }
@@ -149,7 +150,7 @@ struct WorkspaceLayout {
 
 WorkspaceLayout workspace_for(const DecodeParams& p, bool tc) {
   WorkspaceLayout w{0, 0, 0};
-  if (tc) w.rowmap_bytes = align256((int64_t)p.rows * p.rowmap_stride * 4);
+  if (tc) w.rowmap_bytes = align256((int64_t)p.rows * p.rowmap_stride * 4) + align256((int64_t)p.rows * p.num_chunks * 16);
   if (p.num_chunks > 1) {
     const int64_t n = (int64_t)p.rows * p.num_q_heads * p.num_chunks;
     w.part_o_bytes = align256(n * 128 * 4);
@@ -209,7 +210,10 @@ int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t wo
     if (!workspace || (int64_t)workspace_bytes < lay.total()) return QSA_B200_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return QSA_B200_ERR_MISALIGNED;
     char* ws = static_cast<char*>(workspace);
-    if (use_tc) p.rowmap = reinterpret_cast<int32_t*>(ws);
+    if (use_tc) {
+      p.rowmap = reinterpret_cast<int32_t*>(ws);
+      p.tile_flags = reinterpret_cast<uint8_t*>(ws + align256((int64_t)p.rows * p.rowmap_stride * 4));
+    }
     if (p.num_chunks > 1) {
       p.part_o = reinterpret_cast<float*>(ws + lay.rowmap_bytes);
       p.part_lse = reinterpret_cast<float*>(ws + lay.rowmap_bytes + lay.part_o_bytes);

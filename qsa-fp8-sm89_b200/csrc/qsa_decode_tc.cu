@@ -15,10 +15,12 @@
 // travels with the item's metadata slot, and an id of -1 after the last item
 // ends the loaders' and the MMA warp's loops. Four roles overlap across items:
 //
-//   decoder (warp 0)   for a kMeta-deep metadata ring: one TMA bulk copy brings
+//   decoder (warp 0)   for a kMeta-deep metadata ring: TMA bulk copies bring
 //                      the item's chunk of the row map into the slot's row
-//                      table, and the G query heads are split into FP8 terms
-//                      (operand Qs) with their scales;
+//                      table, with the chunk's tile flags (which 128-entry
+//                      tiles hold a valid entry; the others are skipped by
+//                      every role), and the G query heads are split into FP8
+//                      terms (operand Qs) with their scales;
 //   loaders            the ring of 16 KiB tile slots is filled in the order
 //                      the MMA warp drains it: K tiles of item k, then V tiles
 //                      of item k-1. Slot s belongs to loader s % kLoaders, which
@@ -113,7 +115,8 @@ struct Cfg {
   static constexpr int kQs = 0;                                        // [kMeta][NS][128]
   static constexpr int kPs = kQs + kMeta * kQsBytes;                   // [2][kTiles][NO][128]
   static constexpr int kRowTab = kPs + 2 * kPsBytes;                   // int32 [kMeta][kChunk] token slots
-  static constexpr int kQinv = kRowTab + kMeta * kChunk * 4;           // float [kMeta][G]
+  static constexpr int kTileFlags = kRowTab + kMeta * kChunk * 4;      // uint8 [kMeta][16] (kTiles used)
+  static constexpr int kQinv = kTileFlags + kMeta * 16;                // float [kMeta][G]
   static constexpr int kRedMax = align128(kQinv + kMeta * G * 4);      // float [2][8][G]
   static constexpr int kRedSum = align128(kRedMax + 2 * kSoftmaxWarps * G * 4);  // float [2][8][G]
   static constexpr int kBars = align128(kRedSum + 2 * kSoftmaxWarps * G * 4);
@@ -134,7 +137,9 @@ struct Cfg {
   static_assert(kQs % 1024 == 0 && kPs % 1024 == 0 && kSlotBase % 1024 == 0 && kQsBytes % 1024 == 0 &&
                     (NO * 128) % 1024 == 0,
                 "MMA operands must start on 1024-byte swizzle atoms");
-  static_assert(kRowTab % 128 == 0 && kBars % 8 == 0 && kMisc % 8 == 0 && kMeta <= 8, "alignment of the small arrays");
+  static_assert(kRowTab % 128 == 0 && kTileFlags % 16 == 0 && kBars % 8 == 0 && kMisc % 8 == 0 && kMeta <= 8 &&
+                    kTiles <= 16,
+                "alignment of the small arrays");
 };
 
 struct Item {
@@ -148,12 +153,6 @@ __device__ __forceinline__ Item item_of(const DecodeParams& p, int item) {
   it.chunk = rc % p.num_chunks;
   it.row = rc / p.num_chunks;
   return it;
-}
-
-__device__ __forceinline__ int item_tiles(const DecodeParams& p, int chunk, int chunk_tokens) {
-  const int c0 = chunk * chunk_tokens;
-  const int clen = max(0, min(chunk_tokens, p.topk - c0));
-  return (clen + kTile - 1) / kTile;
 }
 
 // ------------------------------------------------------------------ PTX ----
@@ -287,6 +286,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* red_max = reinterpret_cast<float*>(smem + C::kRedMax);
   float* red_sum = reinterpret_cast<float*>(smem + C::kRedSum);
   int32_t* rowtab = reinterpret_cast<int32_t*>(smem + C::kRowTab);
+  const uint8_t* tflags = smem + C::kTileFlags;
+  // bit j: tile j of the item in metadata slot m holds a valid entry
+  auto tile_mask = [&](int m) -> uint32_t {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(tflags + m * 16);
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < C::kTiles; ++j) mask |= ((w >> (8 * j)) & 0xffu) ? (1u << j) : 0u;
+    return mask;
+  };
 
   if (tid == 0) {
     for (int i = 0; i < C::kSlots; ++i) {
@@ -389,9 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the item's chunk of the row map -> row table of slot m (completes on
       // meta_full together with the arrival below)
       if (lane == 0) {
-        mbar_expect_tx(meta_full + m, C::kChunk * 4);
+        mbar_expect_tx(meta_full + m, C::kChunk * 4 + 16);
         bulk_copy_g2s(smem_u32(rowtab + m * C::kChunk),
                       p.rowmap + (int64_t)w.row * p.rowmap_stride + (int64_t)w.chunk * C::kChunk, C::kChunk * 4,
+                      meta_full + m);
+        bulk_copy_g2s(smem_u32(tflags + m * 16), p.tile_flags + ((int64_t)w.row * p.num_chunks + w.chunk) * 16, 16,
                       meta_full + m);
         item_ids[m] = item;
       }
@@ -425,12 +435,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmap_v);
     }
     int pos = 0;
-    auto load_tiles = [&](int m, int g, int ntiles, const CUtensorMap* map) -> bool {
+    auto load_tiles = [&](int m, int g, uint32_t mask, const CUtensorMap* map) -> bool {
       const int32_t* tab = rowtab + m * C::kChunk;
-      for (int j = 0; j < ntiles; ++j, ++pos) {
-        const int s = pos % C::kSlots;
+      #pragma unroll 1  // one copy of the loop body: the warp roles share the instruction cache
+      for (int j = 0; j < C::kTiles; ++j) {
+        if (!((mask >> j) & 1u)) continue;
+        const int s = pos++ % C::kSlots;
         if (s % kLoaders != L) continue;
-        const int fill = pos / C::kSlots;
+        const int fill = (pos - 1) / C::kSlots;
         if (fill > 0 &&
             !__all_sync(0xffffffffu, wait_or_abort(kv_empty + s, (uint32_t)((fill - 1) & 1), abort_flag)))
           return false;
@@ -444,7 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return true;
     };
-    int prev_tiles = 0, prev_g = 0;
+    uint32_t prev_mask = 0;
+    int prev_g = 0;
     bool have_prev = false;
     for (int k = 0; !failed; ++k) {
       const int m = k % kMeta;
@@ -454,13 +467,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int item = item_ids[m];
       const Item w = item_of(p, item >= 0 ? item : 0);
-      if (item >= 0 && !load_tiles(m, w.g, item_tiles(p, w.chunk, C::kChunk), &tmap_k)) {
+      const uint32_t mask = item >= 0 ? tile_mask(m) : 0u;
+      if (item >= 0 && !load_tiles(m, w.g, mask, &tmap_k)) {
         failed = true;
         break;
       }
       if (have_prev) {
         const int m1 = (k - 1) % kMeta;
-        if (!load_tiles(m1, prev_g, prev_tiles, &tmap_v)) {
+        if (!load_tiles(m1, prev_g, prev_mask, &tmap_v)) {
           failed = true;
           break;
         }
@@ -468,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(meta_empty + m1);  // this warp is done with item k-1's row table
       }
       if (item < 0) break;
-      prev_tiles = item_tiles(p, w.chunk, C::kChunk);
+      prev_mask = mask;
       prev_g = w.g;
       have_prev = true;
     }
@@ -482,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ================================= MMA ==================================
     if (lane == 0) {
       int t = 0;  // ring position of the next tile
-      int prev_tiles = 0;
+      uint32_t prev_mask = 0;
       bool have_prev = false;
       for (int k = 0; !failed; ++k) {
         const int m = k % kMeta;
@@ -491,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int item = item_ids[m];
-        const int ntiles = item >= 0 ? item_tiles(p, item_of(p, item).chunk, C::kChunk) : 0;
+        const uint32_t mask = item >= 0 ? tile_mask(m) : 0u;
         if (item >= 0) {
           // S(k) = K tiles of item k . Qs^T
           const int tb = k % kTmemBufs;
@@ -502,12 +516,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t qs0 = base_s + C::kQs + m * C::kQsBytes;
-          for (int j = 0; j < ntiles; ++j, ++t) {
+          #pragma unroll 1  // one copy of the loop body: the warp roles share the instruction cache
+          for (int j = 0; j < C::kTiles; ++j) {
+            if (!((mask >> j) & 1u)) continue;
             const int slot = t % C::kSlots;
             if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
               failed = true;
               break;
             }
+            ++t;
             tc_fence_after();
             const uint32_t a0 = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes;
 #pragma unroll
@@ -533,12 +550,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t d = tmem + tb * C::kBufCols + C::kTiles * C::NS;
-          for (int j = 0; j < prev_tiles; ++j, ++t) {
+          bool first = true;  // the first multiplied tile overwrites the accumulator
+          #pragma unroll 1  // one copy of the loop body: the warp roles share the instruction cache
+          for (int j = 0; j < C::kTiles; ++j) {
+            if (!((prev_mask >> j) & 1u)) continue;
             const int slot = t % C::kSlots;
             if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
               failed = true;
               break;
             }
+            ++t;
             tc_fence_after();
             const uint32_t a0 = base_s + C::kSlotBase + (uint32_t)slot * kTileBytes;
             const uint32_t b0 = base_s + C::kPs + pb * C::kPsBytes + j * C::NO * 128;
@@ -546,15 +567,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < kTile / 32; ++kk) {
               const uint64_t ad = smem_desc_sw128(a0 + kk * 32 * 128, kTileBytes, 1024);
               const uint64_t bd = smem_desc_sw128(b0 + kk * 32, 16, 1024);
-              mma_f8(d, ad, bd, C::kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+              mma_f8(d, ad, bd, C::kIdescO, (!first || kk > 0) ? 1u : 0u);
             }
+            first = false;
             mma_commit(kv_empty + slot);
           }
           if (failed) break;
           mma_commit(o_full + tb);
         }
         if (item < 0) break;
-        prev_tiles = ntiles;
+        prev_mask = mask;
         have_prev = true;
       }
     }
@@ -579,7 +601,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // O columns this warp loads: the NOH-column block holding its heads' terms
     const int ocol0 = C::NO > C::NOH ? half * C::NOH : 0;
     // state of the item whose epilogue is pending
-    int e_k = -1, e_row = 0, e_g = 0, e_chunk = 0, e_ntiles = 0;
+    int e_k = -1, e_row = 0, e_g = 0, e_chunk = 0;
+    bool e_any = false;  // the pending item has a valid tile
     float e_m[C::kHalfHeads], e_l[C::kHalfHeads];
     __nv_bfloat16 e_gate[C::kHalfHeads];
     auto epilogue = [&]() {
@@ -596,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
         const int h = h0 + hh;
-        const float o = (e_ntiles > 0 && e_l[hh] > 0.f)
+        const float o = (e_any && e_l[hh] > 0.f)
                             ? combine_p(v + h * kTermsP - ocol0) * (1.0f / 256.0f) / e_l[hh]
                             : 0.f;
         const int64_t hrow = (int64_t)e_row * p.num_q_heads + e_g * G + h;
@@ -615,7 +638,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pb = k & 1;
       const int m = k % kMeta;
       const Item w = item_of(p, item_at(k));
-      const int ntiles = item_tiles(p, w.chunk, C::kChunk);
       // the gate of this warp's heads, needed by the epilogue one iteration later
       __nv_bfloat16 gate[C::kHalfHeads];
       if (p.num_chunks == 1 && has_heads) {
@@ -632,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         failed = !__all_sync(0xffffffffu, ok);
       }
       tc_fence_after();
+      const uint32_t mask = tile_mask(m);
       float qi[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) qi[h] = qinv[m * G + h];
@@ -642,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int jj = 0; jj < C::kHalfTiles; ++jj) {
         const int j = j0 + jj;
-        const bool ok = !failed && j < ntiles && rowtab[m * C::kChunk + j * kTile + tk] >= 0;
+        const bool ok = !failed && ((mask >> j) & 1u) && rowtab[m * C::kChunk + j * kTile + tk] >= 0;
 #pragma unroll
         for (int h = 0; h < G; ++h) sc[jj][h] = ok ? combine_q(&raw[jj * C::NS + h * kTermsQ]) * qi[h] : -INFINITY;
       }
@@ -683,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int jj = 0; jj < C::kHalfTiles; ++jj) {
         const int j = j0 + jj;
-        if (j < ntiles) {
+        if ((mask >> j) & 1u) {
           uint8_t* pt = ps + j * C::NO * 128;
 #pragma unroll
           for (int h = 0; h < G; h += 2) {
@@ -708,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       e_row = w.row;
       e_g = w.g;
       e_chunk = w.chunk;
-      e_ntiles = ntiles;
+      e_any = mask != 0;
 #pragma unroll
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
         const int h = min(h0 + hh, G - 1);
@@ -785,6 +808,21 @@ __global__ void __launch_bounds__(kRowmapThreads) qsa_rowmap_kernel(const __grid
       *reinterpret_cast<int4*>(p.rowmap + (int64_t)row[b] * p.rowmap_stride + col0[b]) =
           make_int4((int)token_slot_from(p, ph[b][0], po[b][0]), (int)token_slot_from(p, ph[b][1], po[b][1]),
                     (int)token_slot_from(p, ph[b][2], po[b][2]), (int)token_slot_from(p, ph[b][3], po[b][3]));
+  // tile flags: the 32 quads of a warp are one 128-entry tile of one row
+  // (rows are whole tiles long), so the warp votes whether the tile holds a
+  // valid entry
+  bool any_valid = false;
+#pragma unroll
+  for (int b = 0; b < kRowmapBatch; ++b)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) any_valid |= row[b] >= 0 && token_slot_from(p, ph[b][e], po[b][e]) >= 0;
+  any_valid = __any_sync(0xffffffffu, any_valid);
+  if ((threadIdx.x & 31) == 0 && row[0] >= 0) {
+    const int tile = col0[0] / 128;
+    const int tiles_per_chunk = p.chunk_tokens / 128;
+    p.tile_flags[((int64_t)row[0] * p.num_chunks + tile / tiles_per_chunk) * 16 + tile % tiles_per_chunk] =
+        any_valid ? 1 : 0;
+  }
   // the decode kernel reads the map through TMA (the async proxy)
   fence_proxy_async_global();
 }
@@ -846,7 +884,7 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
   if (p.num_pages * p.page_size * p.num_kv_heads > 0x7fffffffll) return cudaErrorInvalidValue;
-  if (!p.rowmap || p.rowmap_stride != p.num_chunks * C::kChunk) return cudaErrorInvalidValue;
+  if (!p.rowmap || !p.tile_flags || p.rowmap_stride != p.num_chunks * C::kChunk) return cudaErrorInvalidValue;
   const int64_t rows = p.num_pages * p.page_size * p.num_kv_heads;
   CUtensorMap mk, mv;
   if (!encode_rows(&mk, p.k, rows) || !encode_rows(&mv, p.v, rows)) return cudaErrorInvalidValue;

@@ -53,6 +53,10 @@ struct DecodeParams {
   // past topk -1).
   int32_t* rowmap;
   int rowmap_stride;
+  // Tile flags (workspace, filled with the row map): one byte per 128-entry
+  // tile of each (row, chunk), nonzero when the tile holds a valid entry;
+  // 16 bytes per (row, chunk).
+  uint8_t* tile_flags;
 
   int* err;  // device error word of the current device
 };
