@@ -76,17 +76,10 @@ constexpr int kDecoderWarp = 0;
 constexpr int kLoaders = 6;                   // loader warps 1 .. kLoaders
 constexpr int kMmaWarp = 1 + kLoaders;
 constexpr int kSoftmax0 = kMmaWarp + 1;       // softmax / epilogue warps
-constexpr int kSoftmaxWarps = 4;              // 4 or 8: one or two per TMEM lane quadrant
-constexpr int kSoftmaxSets = kSoftmaxWarps / 4;
-// 12 warps, one CTA per SM: up to 168 registers per thread (each SM
-// sub-partition has 16K registers and holds a quarter of the warps)
-constexpr int kThreads = 32 * (kSoftmax0 + kSoftmaxWarps);
-static_assert(kSoftmaxWarps == 4 || kSoftmaxWarps == 8, "softmax warp count");
 static_assert(kSoftmax0 % 4 == 0, "softmax warps must cover the four TMEM lane quadrants in order");
 constexpr int kSmemLimit = 232448;            // 227 KiB opt-in per CTA
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr int kErrTimeout = 1;
-static_assert(kThreads % 128 == 0, "whole warpgroups, so the four sub-partitions hold equal shares");
 
 __host__ __device__ constexpr int align128(int x) { return (x + 127) / 128 * 128; }
 
@@ -98,6 +91,15 @@ __host__ __device__ constexpr int pow2_at_least(int x) {
 
 template <int G>
 struct Cfg {
+  // softmax / epilogue warps: one per TMEM lane quadrant, or two (each taking
+  // half of the score tiles and half of the heads) where G >= 8 makes the
+  // per-item softmax longer than the item's K/V transfer. 12 warps leave up to
+  // 168 registers a thread, 16 warps 128 (one CTA per SM; an SM sub-partition
+  // has 16K registers and holds a quarter of the warps).
+  static constexpr int kSoftmaxWarps = G >= 8 ? 8 : 4;
+  static constexpr int kSoftmaxSets = kSoftmaxWarps / 4;
+  static constexpr int kThreads = 32 * (kSoftmax0 + kSoftmaxWarps);
+  static_assert(kThreads % 128 == 0, "whole warpgroups, so the four sub-partitions hold equal shares");
   static constexpr int NS = ((G * kTermsQ + 15) / 16) * 16;  // N of the S MMA (rows of Qs)
   static constexpr int NO = ((G * kTermsP + 15) / 16) * 16;  // N of the O MMA (rows of a Ps tile)
   static constexpr int kTiles = G <= 8 ? 4 : 2;             // tiles per item
@@ -108,7 +110,7 @@ struct Cfg {
   static_assert(kTiles * NS == 64 && (NO == 16 || NO == 32 || NO == 64), "TMEM load widths");
   static constexpr int kHalfTiles = kTiles / kSoftmaxSets;                    // score tiles per softmax warp
   static constexpr int kHalfHeads = G >= kSoftmaxSets ? G / kSoftmaxSets : 1;  // epilogue heads per softmax warp
-  static constexpr int NOH = NO > 16 ? NO / kSoftmaxSets : 16;                 // O columns one softmax warp loads
+  static constexpr int kHeadCols = kHalfHeads * kTermsP;                       // O columns one softmax warp loads
   static constexpr int kPsBytes = kTiles * NO * 128;
   // shared memory layout (offsets from a 1024-byte aligned base); every
   // region starts on a 128-byte boundary, the MMA operands on 1024
@@ -117,8 +119,8 @@ struct Cfg {
   static constexpr int kRowTab = kPs + 2 * kPsBytes;                   // int32 [kMeta][kChunk] token slots
   static constexpr int kTileFlags = kRowTab + kMeta * kChunk * 4;      // uint8 [kMeta][16] (kTiles used)
   static constexpr int kQinv = kTileFlags + kMeta * 16;                // float [kMeta][G]
-  static constexpr int kRedMax = align128(kQinv + kMeta * G * 4);      // float [2][8][G]
-  static constexpr int kRedSum = align128(kRedMax + 2 * kSoftmaxWarps * G * 4);  // float [2][8][G]
+  static constexpr int kRedMax = align128(kQinv + kMeta * G * 4);      // float [2][kSoftmaxWarps][G]
+  static constexpr int kRedSum = align128(kRedMax + 2 * kSoftmaxWarps * G * 4);  // float [2][kSoftmaxWarps][G]
   static constexpr int kBars = align128(kRedSum + 2 * kSoftmaxWarps * G * 4);
   static constexpr int kMaxSlots = 16;
   static constexpr int kNumBars = 2 * kMaxSlots + 2 * kMeta + 3 * kTmemBufs + 2;
@@ -253,7 +255,7 @@ __device__ __forceinline__ float combine_p(const float* v) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     qsa_decode_tc_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
                          const __grid_constant__ CUtensorMap tmap_v, int num_items) {
   using C = Cfg<G>;
@@ -308,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < kTmemBufs; ++b) {
       mbar_init(s_full + b, 1);
       mbar_init(o_full + b, 1);
-      mbar_init(tmem_empty + b, 32 * kSoftmaxWarps);
+      mbar_init(tmem_empty + b, 32 * C::kSoftmaxWarps);
     }
     for (int b = 0; b < 2; ++b) mbar_init(p_full + b, 1);
     *abort_flag = 0;
@@ -589,17 +591,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Software pipelined: the softmax of item k runs before the epilogue of
     // item k-1, whose O accumulation has finished meanwhile. With two sets of
     // softmax warps, warps sw and sw + 4 share a TMEM lane quadrant and `half`
-    // picks their score tiles and epilogue heads.
+    // picks their score tiles and epilogue heads (it only offsets addresses:
+    // every register array is indexed by compile-time constants).
     const int q4 = warp & 3;                // TMEM lane quadrant of this warp
-    const int sw = warp - kSoftmax0;        // 0 .. kSoftmaxWarps-1
-    const int half = kSoftmaxSets > 1 ? (sw >> 2) : 0;  // softmax set
+    const int sw = warp - kSoftmax0;        // 0 .. C::kSoftmaxWarps-1
+    const int half = C::kSoftmaxSets > 1 ? (sw >> 2) : 0;  // softmax set
     const int tk = q4 * 32 + lane;          // token within a tile / head dim in the epilogue
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const int j0 = half * C::kHalfTiles;    // first score tile of this warp
     const int h0 = half * C::kHalfHeads;    // first epilogue head of this warp
     const bool has_heads = h0 < G;          // false only for the second half when G == 1
-    // O columns this warp loads: the NOH-column block holding its heads' terms
-    const int ocol0 = C::NO > C::NOH ? half * C::NOH : 0;
     // state of the item whose epilogue is pending
     int e_k = -1, e_row = 0, e_g = 0, e_chunk = 0;
     bool e_any = false;  // the pending item has a valid tile
@@ -611,8 +612,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + tb, (uint32_t)((e_k / kTmemBufs) & 1), abort_flag));
       if (failed) return;
       tc_fence_after();
-      float v[C::NOH];
-      tmem_ld_wait<C::NOH>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + ocol0, v);
+      // the O columns of this warp's heads (their kTermsP terms each)
+      float v[C::kHeadCols];
+      if (has_heads)
+        tmem_ld_wait<C::kHeadCols>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + h0 * kTermsP, v);
       tc_fence_before();
       mbar_arrive(tmem_empty + tb);
       if (!has_heads) return;
@@ -620,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
         const int h = h0 + hh;
         const float o = (e_any && e_l[hh] > 0.f)
-                            ? combine_p(v + h * kTermsP - ocol0) * (1.0f / 256.0f) / e_l[hh]
+                            ? combine_p(v + hh * kTermsP) * (1.0f / 256.0f) / e_l[hh]
                             : 0.f;
         const int64_t hrow = (int64_t)e_row * p.num_q_heads + e_g * G + h;
         if (p.num_chunks == 1) {
@@ -677,17 +680,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int jj = 1; jj < C::kHalfTiles; ++jj) mx = fmaxf(mx, sc[jj][h]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) red_max[(pb * kSoftmaxWarps + sw) * G + h] = mx;
+        if (lane == 0) red_max[(pb * C::kSoftmaxWarps + sw) * G + h] = mx;
       }
-      named_bar_sync(1, 32 * kSoftmaxWarps);
+      named_bar_sync(1, 32 * C::kSoftmaxWarps);
       if (sw == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // row table and scales read
       float m_h[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float* rm = red_max + pb * kSoftmaxWarps * G + h;
+        const float* rm = red_max + pb * C::kSoftmaxWarps * G + h;
         float mx = rm[0];
 #pragma unroll
-        for (int i = 1; i < kSoftmaxWarps; ++i) mx = fmaxf(mx, rm[i * G]);
+        for (int i = 1; i < C::kSoftmaxWarps; ++i) mx = fmaxf(mx, rm[i * G]);
         m_h[h] = mx;
         float sum = 0.f;
 #pragma unroll
@@ -698,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) red_sum[(pb * kSoftmaxWarps + sw) * G + h] = sum;
+        if (lane == 0) red_sum[(pb * C::kSoftmaxWarps + sw) * G + h] = sum;
       }
       // probabilities -> FP8 terms of p*256 (row h*kTermsP+j of Ps, one byte per
       // token), two heads per conversion
@@ -722,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       fence_proxy_async_smem();
-      named_bar_sync(1, 32 * kSoftmaxWarps);
+      named_bar_sync(1, 32 * C::kSoftmaxWarps);
       if (sw == 0 && lane == 0 && !failed) mbar_arrive(p_full + pb);
 
       // ---- epilogue of the previous item, then this item becomes pending ---
@@ -734,12 +737,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       e_any = mask != 0;
 #pragma unroll
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
+        // this warp's heads, read back from the group's partials (a head index
+        // that is not a compile-time constant must not index a register array)
         const int h = min(h0 + hh, G - 1);
-        const float* rs = red_sum + pb * kSoftmaxWarps * G + h;
-        float l = 0.f;
+        const float* rs = red_sum + pb * C::kSoftmaxWarps * G + h;
+        const float* rm = red_max + pb * C::kSoftmaxWarps * G + h;
+        float l = 0.f, mx = rm[0];
 #pragma unroll
-        for (int i = 0; i < kSoftmaxWarps; ++i) l += rs[i * G];
-        e_m[hh] = m_h[h];
+        for (int i = 0; i < C::kSoftmaxWarps; ++i) {
+          l += rs[i * G];
+          mx = fmaxf(mx, rm[i * G]);
+        }
+        e_m[hh] = mx;
         e_l[hh] = l;
         e_gate[hh] = (p.num_chunks == 1 && has_heads) ? gate[hh] : __float2bfloat16_rn(0.f);
       }
@@ -898,7 +907,7 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3((unsigned)kThreads);
+  cfg.blockDim = dim3((unsigned)C::kThreads);
   cfg.dynamicSmemBytes = (size_t)C::kSmemAlloc;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
