@@ -23,6 +23,11 @@
  *   - the eager oracle    torch_eager(...)       sm89_torch.py:27-54
  *   - the Triton launch   launch(q, k, v, indices, btable, t2r, gate, out,
  *                          k_scale, v_scale)     sm89_triton.py:118-142
+ *   - the cache producer  (randn * 0.1).to(float8_e4m3fn) into the paged
+ *                          [num_pages, P, Hkv, 128] layout, with the scales
+ *                          returned beside it    sm89_cutedsl.py:48-62, :79
+ *                          (qsa_b200_cache_write: the same layout, written
+ *                          at given token slots, saturating at +-448)
  */
 #ifndef QSA_B200_H_
 #define QSA_B200_H_
@@ -55,7 +60,8 @@ enum {
   QSA_B200_ERR_DEVICE = -6,       /* current device is not sm_100 */
   QSA_B200_ERR_LAUNCH = -7,       /* the CUDA launch itself failed */
   QSA_B200_ERR_KERNEL = -8,       /* a kernel reported a device-side failure */
-  QSA_B200_ERR_TOO_LARGE = -9     /* workspace above the fixed scratch of qsa_b200_decode_noalloc */
+  QSA_B200_ERR_TOO_LARGE = -9,    /* workspace above the fixed scratch of qsa_b200_decode_noalloc */
+  QSA_B200_ERR_BAD_VALUE = -10    /* a scale is not a positive finite number */
 };
 
 /* Kernel selection. AUTO picks the tensor-core kernel for group sizes
@@ -165,6 +171,38 @@ QSA_B200_API int qsa_b200_abi_version(void);
  *   - Calls that overlap in time on one device (other streams or threads)
  *     share the scratch and race; the caller serialises them. */
 QSA_B200_API int qsa_b200_decode_noalloc(const qsa_b200_decode_args* args, qsa_b200_stream_t stream);
+
+/* Element types of the new keys and values of qsa_b200_cache_write. */
+enum { QSA_B200_DTYPE_BF16 = 0, QSA_B200_DTYPE_F16 = 1, QSA_B200_DTYPE_F32 = 2 };
+
+typedef struct qsa_b200_cache_write_args {
+  const void* k;         /* new keys [tokens, num_kv_heads, head_dim] of input_dtype */
+  const void* v;         /* new values, same shape, type and strides as k */
+  const int64_t* slots;  /* [tokens]: physical token slot phys_page * page_size + offset of each token;
+                            a negative slot or one past the cache is skipped */
+  void* k_cache;         /* fp8 e4m3fn [num_pages, page_size, num_kv_heads, head_dim] */
+  void* v_cache;         /* same layout as k_cache */
+  float k_scale;         /* dequantisation scales (cache value * scale = stored value) */
+  float v_scale;
+  int32_t tokens;
+  int32_t num_kv_heads;
+  int32_t head_dim;      /* must be 128 */
+  int32_t page_size;
+  int64_t num_pages;
+  int64_t token_stride;  /* elements from one token of k / v to the next, >= num_kv_heads * head_dim */
+  int32_t input_dtype;   /* QSA_B200_DTYPE_* */
+} qsa_b200_cache_write_args;
+
+/* Quantises new keys and values into the paged FP8 caches:
+ *   cache[slot, g, d] = e4m3fn(x[t, g, d] / scale)   for slot = slots[t]
+ * with x / scale an IEEE fp32 division and the conversion rounding to the
+ * nearest E4M3FN value (ties to even), saturating at +-448: a finite value
+ * beyond the range and an infinity become +-448, NaN stays NaN (torch's cast
+ * turns |x| >= 464 into NaN instead). Rows of skipped tokens are left as they
+ * were. Two tokens with the same slot race (the caller gives each slot once).
+ * Needs k, v 16-byte aligned with token_stride * element size a multiple of
+ * 16, and 16-byte aligned caches. Asynchronous on `stream`. */
+QSA_B200_API int qsa_b200_cache_write(const qsa_b200_cache_write_args* args, qsa_b200_stream_t stream);
 
 #ifdef __cplusplus
 }

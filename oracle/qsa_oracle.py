@@ -43,6 +43,7 @@ __all__ = [
     "bf16_to_f32",
     "f32_to_bf16",
     "f32_to_e4m3fn_sat",
+    "cache_write",
     "decode_slots",
     "attention",
     "attention_bf16",
@@ -116,6 +117,32 @@ def f32_to_e4m3fn_sat(x: np.ndarray) -> np.ndarray:
     code = np.where(neg, code | np.uint8(0x80), code).astype(np.uint8)
     code = np.where(np.isnan(x), np.uint8(0x7F), code).astype(np.uint8)
     return code
+
+
+def cache_write(k_cache, v_cache, k_new, v_new, slots, k_scale, v_scale):
+    """The paged cache producer: new keys / values quantised into the FP8
+    caches at physical token slots; returns updated copies of the caches.
+
+    The reference fills its caches with ``(randn * 0.1).to(float8_e4m3fn)``
+    in the ``[num_pages, P, Hkv, 128]`` layout and dequantises them as
+    ``value * scale`` (sm89_cutedsl.py:48-62, :79; sm89_torch.py:43-44). The
+    writer stores ``e4m3fn(x / scale)``: an IEEE float32 division, then
+    :func:`f32_to_e4m3fn_sat` (nearest, ties to even, saturating at +-448,
+    NaN kept). ``k_cache``/``v_cache`` are uint8 byte arrays, ``k_new``/
+    ``v_new`` float32 ``[tokens, Hkv, 128]`` (bf16 / fp16 inputs converted
+    exactly beforehand), ``slots`` int ``[tokens]``: ``phys_page * P +
+    offset``; a negative slot or one past the cache is skipped.
+    """
+    kc = np.array(k_cache, dtype=np.uint8, copy=True)
+    vc = np.array(v_cache, dtype=np.uint8, copy=True)
+    npages, page, hkv, d = kc.shape
+    s = np.asarray(slots, dtype=np.int64)
+    ok = (s >= 0) & (s < npages * page)
+    kq = f32_to_e4m3fn_sat(np.asarray(k_new, dtype=np.float32)[ok] / np.float32(k_scale))
+    vq = f32_to_e4m3fn_sat(np.asarray(v_new, dtype=np.float32)[ok] / np.float32(v_scale))
+    kc.reshape(npages * page, hkv, d)[s[ok]] = kq
+    vc.reshape(npages * page, hkv, d)[s[ok]] = vq
+    return kc, vc
 
 
 def decode_slots(

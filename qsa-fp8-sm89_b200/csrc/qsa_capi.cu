@@ -181,6 +181,7 @@ const char* qsa_b200_status_string(int status) {
     case QSA_B200_ERR_KERNEL: return "a kernel reported a device-side failure";
     case QSA_B200_ERR_TOO_LARGE:
       return "workspace needed exceeds QSA_B200_NOALLOC_SCRATCH_BYTES (use qsa_b200_decode with a workspace)";
+    case QSA_B200_ERR_BAD_VALUE: return "a scale is not a positive finite number";
     default: return "unknown status";
   }
 }
@@ -283,6 +284,41 @@ void launch_qsa_cuda(const void* q, const void* k, const void* v, const void* in
   // This signature takes no workspace: the row map (and any split partials)
   // go to the library's fixed per-device scratch.
   t_last_status = qsa_b200_decode_noalloc(&a, stream);
+}
+
+int qsa_b200_cache_write(const qsa_b200_cache_write_args* a, qsa_b200_stream_t stream) {
+  if (!a) return QSA_B200_ERR_NULL_POINTER;
+  if (a->tokens < 0 || a->num_kv_heads < 1 || a->page_size < 1 || a->num_pages < 1) return QSA_B200_ERR_BAD_SHAPE;
+  if (a->head_dim != 128) return QSA_B200_ERR_UNSUPPORTED;
+  if (a->input_dtype < QSA_B200_DTYPE_BF16 || a->input_dtype > QSA_B200_DTYPE_F32) return QSA_B200_ERR_UNSUPPORTED;
+  if (!(a->k_scale > 0.f) || !(a->v_scale > 0.f) || !std::isfinite(a->k_scale) || !std::isfinite(a->v_scale))
+    return QSA_B200_ERR_BAD_VALUE;
+  const int64_t row_elems = (int64_t)a->num_kv_heads * a->head_dim;
+  if (a->token_stride < row_elems) return QSA_B200_ERR_BAD_SHAPE;
+  if (a->tokens == 0) return QSA_B200_OK;
+  if (!a->k || !a->v || !a->slots || !a->k_cache || !a->v_cache) return QSA_B200_ERR_NULL_POINTER;
+  const int64_t elem = a->input_dtype == QSA_B200_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(a->k) || !aligned16(a->v) || !aligned16(a->k_cache) || !aligned16(a->v_cache) ||
+      (a->token_stride * elem) % 16 != 0 || (reinterpret_cast<uintptr_t>(a->slots) & 7u))
+    return QSA_B200_ERR_MISALIGNED;
+  const int st = check_device();
+  if (st != QSA_B200_OK) return st;
+  CacheWriteParams p;
+  p.k = a->k;
+  p.v = a->v;
+  p.slots = a->slots;
+  p.k_cache = static_cast<uint8_t*>(a->k_cache);
+  p.v_cache = static_cast<uint8_t*>(a->v_cache);
+  p.k_scale = a->k_scale;
+  p.v_scale = a->v_scale;
+  p.tokens = a->tokens;
+  p.num_kv_heads = a->num_kv_heads;
+  p.page_size = a->page_size;
+  p.num_pages = a->num_pages;
+  p.token_stride = a->token_stride;
+  p.dtype = a->input_dtype;
+  const cudaError_t e = launch_cache_write(p, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? QSA_B200_OK : QSA_B200_ERR_LAUNCH;
 }
 
 int qsa_b200_last_status(void) { return t_last_status; }

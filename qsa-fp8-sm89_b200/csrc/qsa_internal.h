@@ -66,6 +66,22 @@ cudaError_t launch_decode_tc(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_decode_simt(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream);
 cudaError_t launch_slots(const DecodeParams& p, int64_t* slots, cudaStream_t stream);
+// Paged FP8 cache writer (qsa_cache_write.cu).
+struct CacheWriteParams {
+  const void* k;  // [tokens, Hkv, 128] new keys, rows token_stride elements apart
+  const void* v;
+  const int64_t* slots;  // [tokens] physical token slots; outside [0, num_pages * P) = skipped
+  uint8_t* k_cache;      // [num_pages, P, Hkv, 128] e4m3fn
+  uint8_t* v_cache;
+  float k_scale, v_scale;
+  int tokens;
+  int num_kv_heads;
+  int page_size;
+  int64_t num_pages;
+  int64_t token_stride;
+  int dtype;  // QSA_B200_DTYPE_*
+};
+cudaError_t launch_cache_write(const CacheWriteParams& p, cudaStream_t stream);
 
 // Top-K entries per work item for a GQA group size (both kernels split rows
 // the same way, so the workspace size depends only on the shape), and the

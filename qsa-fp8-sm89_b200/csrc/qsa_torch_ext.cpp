@@ -138,6 +138,53 @@ void slots(const at::Tensor& btable, const std::optional<at::Tensor>& t2r, const
   TORCH_CHECK(st == QSA_B200_OK, "qsa_b200_slots failed: ", qsa_b200_status_string(st));
 }
 
+void cache_write(const at::Tensor& k_new, const at::Tensor& v_new, const at::Tensor& slots_t, double k_scale,
+                 double v_scale, at::Tensor& k_cache, at::Tensor& v_cache) {
+  TORCH_CHECK(k_new.is_cuda(), "k_new must be a CUDA tensor");
+  int32_t dtype = -1;
+  if (k_new.scalar_type() == at::kBFloat16) dtype = QSA_B200_DTYPE_BF16;
+  if (k_new.scalar_type() == at::kHalf) dtype = QSA_B200_DTYPE_F16;
+  if (k_new.scalar_type() == at::kFloat) dtype = QSA_B200_DTYPE_F32;
+  TORCH_CHECK(dtype >= 0, "k_new must be bfloat16, float16 or float32, got ", k_new.scalar_type());
+  TORCH_CHECK(v_new.scalar_type() == k_new.scalar_type(), "v_new must have k_new's dtype");
+  TORCH_CHECK(k_new.dim() == 3 && k_new.stride(2) == 1 && k_new.stride(1) == k_new.size(2),
+              "k_new must be [tokens, Hkv, D] with contiguous heads");
+  TORCH_CHECK(v_new.sizes() == k_new.sizes() && v_new.strides() == k_new.strides(),
+              "v_new must have k_new's shape and strides");
+  TORCH_CHECK(slots_t.scalar_type() == at::kLong && slots_t.dim() == 1 && slots_t.size(0) == k_new.size(0) &&
+                  slots_t.is_contiguous(),
+              "slots must be contiguous int64 [tokens]");
+  TORCH_CHECK(k_cache.scalar_type() == at::kFloat8_e4m3fn || k_cache.scalar_type() == at::kByte,
+              "k_cache must be float8_e4m3fn (or its uint8 bytes)");
+  TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "v_cache must have k_cache's dtype");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes() &&
+                  v_cache.is_contiguous(),
+              "k_cache / v_cache must be contiguous [pages, P, Hkv, D]");
+  TORCH_CHECK(k_cache.size(2) == k_new.size(1) && k_cache.size(3) == k_new.size(2),
+              "heads / head_dim of the new rows and the cache differ");
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&v_new, &slots_t, &k_cache, &v_cache})
+    TORCH_CHECK(t->device() == k_new.device(), "all tensors must be on k_new's device");
+  c10::cuda::CUDAGuard guard(k_new.device());
+  qsa_b200_cache_write_args a = {};
+  a.k = k_new.data_ptr();
+  a.v = v_new.data_ptr();
+  a.slots = slots_t.data_ptr<int64_t>();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.k_scale = (float)k_scale;
+  a.v_scale = (float)v_scale;
+  a.tokens = (int32_t)k_new.size(0);
+  a.num_kv_heads = (int32_t)k_cache.size(2);
+  a.head_dim = (int32_t)k_cache.size(3);
+  a.page_size = (int32_t)k_cache.size(1);
+  a.num_pages = k_cache.size(0);
+  a.token_stride = k_new.size(0) > 1 ? k_new.stride(0) : k_new.size(1) * k_new.size(2);
+  a.input_dtype = dtype;
+  const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(k_new.device().index()).stream();
+  const int st = qsa_b200_cache_write(&a, reinterpret_cast<qsa_b200_stream_t>(stream));
+  TORCH_CHECK(st == QSA_B200_OK, "qsa_b200_cache_write failed: ", qsa_b200_status_string(st));
+}
+
 }  // namespace
 
 TORCH_LIBRARY(qsa_b200, m) {
@@ -148,9 +195,13 @@ TORCH_LIBRARY(qsa_b200, m) {
   m.def(
       "slots(Tensor btable, Tensor? t2r, Tensor indices, Tensor? counts, bool count_column, int topk, "
       "int page_size, int num_pages, Tensor(a!) out) -> ()");
+  m.def(
+      "cache_write(Tensor k_new, Tensor v_new, Tensor slots, float k_scale, float v_scale, Tensor(a!) k_cache, "
+      "Tensor(b!) v_cache) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(qsa_b200, CUDA, m) {
   m.impl("decode", &decode);
   m.impl("slots", &slots);
+  m.impl("cache_write", &cache_write);
 }

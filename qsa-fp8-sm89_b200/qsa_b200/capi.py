@@ -26,6 +26,7 @@ ERR_DEVICE = -6
 ERR_LAUNCH = -7
 ERR_KERNEL = -8
 ERR_TOO_LARGE = -9
+ERR_BAD_VALUE = -10
 
 # Fixed split scratch of qsa_b200_decode_noalloc (QSA_B200_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
@@ -33,6 +34,10 @@ NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 KERNEL_AUTO = 0
 KERNEL_TC = 1
 KERNEL_SIMT = 2
+
+DTYPE_BF16 = 0
+DTYPE_F16 = 1
+DTYPE_F32 = 2
 
 LOG2E = 1.4426950408889634
 
@@ -47,6 +52,7 @@ EXPORTED = (
     "qsa_b200_status_string",
     "qsa_b200_abi_version",
     "qsa_b200_decode_noalloc",
+    "qsa_b200_cache_write",
 )
 
 
@@ -82,6 +88,27 @@ class DecodeArgs(ctypes.Structure):
     ]
 
 
+class CacheWriteArgs(ctypes.Structure):
+    """Mirror of ``qsa_b200_cache_write_args``."""
+
+    _fields_ = [
+        ("k", c_void_p),
+        ("v", c_void_p),
+        ("slots", c_void_p),
+        ("k_cache", c_void_p),
+        ("v_cache", c_void_p),
+        ("k_scale", c_float),
+        ("v_scale", c_float),
+        ("tokens", c_int32),
+        ("num_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("page_size", c_int32),
+        ("num_pages", c_int64),
+        ("token_stride", c_int64),
+        ("input_dtype", c_int32),
+    ]
+
+
 _configured = False
 
 
@@ -109,6 +136,8 @@ def lib() -> ctypes.CDLL:
         L.qsa_b200_abi_version.restype = c_int
         L.qsa_b200_decode_noalloc.argtypes = [P, c_void_p]
         L.qsa_b200_decode_noalloc.restype = c_int
+        L.qsa_b200_cache_write.argtypes = [ctypes.POINTER(CacheWriteArgs), c_void_p]
+        L.qsa_b200_cache_write.restype = c_int
         _configured = True
     return L
 
@@ -184,6 +213,33 @@ def launch_qsa_cuda(q, k, v, indices, btable, t2r, gate, out, k_scale, v_scale, 
         c_int32(k.shape[2]), c_int32(indices.shape[1] - 1), c_int32(k.shape[1]), c_int32(max_pages),
         c_int32(hd), c_int32(q.shape[1] // k.shape[2]), c_void_p(stream))
     return int(L.qsa_b200_last_status())
+
+
+_DTYPES = {"torch.bfloat16": DTYPE_BF16, "torch.float16": DTYPE_F16, "torch.float32": DTYPE_F32}
+
+
+def make_cache_write_args(k_new, v_new, slots, k_cache, v_cache, k_scale=1.0, v_scale=1.0) -> CacheWriteArgs:
+    """Fills ``qsa_b200_cache_write_args`` from torch tensors: new keys and
+    values ``[tokens, Hkv, 128]`` (bf16, fp16 or fp32, unit stride inside a
+    token), int64 ``slots[tokens]``, caches ``[num_pages, P, Hkv, 128]``. No
+    checks: the C side validates."""
+    a = CacheWriteArgs()
+    a.k, a.v, a.slots = _ptr(k_new), _ptr(v_new), _ptr(slots)
+    a.k_cache, a.v_cache = _ptr(k_cache), _ptr(v_cache)
+    a.k_scale, a.v_scale = float(k_scale), float(v_scale)
+    a.tokens = int(k_new.shape[0])
+    a.num_kv_heads = int(k_cache.shape[2])
+    a.head_dim = int(k_cache.shape[3])
+    a.page_size = int(k_cache.shape[1])
+    a.num_pages = int(k_cache.shape[0])
+    a.token_stride = int(k_new.stride(0))
+    a.input_dtype = _DTYPES.get(str(k_new.dtype), -1)
+    return a
+
+
+def cache_write(args: CacheWriteArgs, stream: int = 0) -> int:
+    """Calls ``qsa_b200_cache_write``; returns its status."""
+    return int(lib().qsa_b200_cache_write(ctypes.byref(args), c_void_p(stream)))
 
 
 def device_error(clear: bool = False) -> int:

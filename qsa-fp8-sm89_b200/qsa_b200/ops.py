@@ -113,6 +113,41 @@ def slots(indices, btable, t2r, page_size, num_pages, counts=None, *, count_colu
     return out
 
 
+def qsa_cache_write(k_new, v_new, slots, k_scale, v_scale, k_cache, v_cache):
+    """Writes new keys and values into the paged FP8 caches the decode reads:
+    ``cache[slot, g, :] = e4m3fn(x[t, g, :] / scale)`` for ``slot =
+    slots[t]`` (``phys_page * P + offset``), in place, asynchronous on the
+    current stream.
+
+    The layout and the scale convention are the reference's cache producer
+    (sm89_cutedsl.py:48-62: ``[num_pages, P, Hkv, 128]`` E4M3FN, dequantised
+    as ``value * scale``). The quotient is an IEEE fp32 division, rounded to
+    the nearest E4M3FN value (ties to even) and saturated at +-448: a finite
+    value beyond the range or an infinity becomes +-448 and NaN stays NaN,
+    where ``torch``'s cast gives NaN for ``|x| >= 464``. Negative slots and
+    slots past the cache are skipped.
+
+    Args:
+        k_new, v_new: bf16, fp16 or fp32 ``[tokens, Hkv, 128]``, heads
+            contiguous (a token stride is allowed).
+        slots: int64 ``[tokens]``.
+        k_scale, v_scale: positive dequantisation scales.
+        k_cache, v_cache: float8_e4m3fn (or uint8) ``[num_pages, P, Hkv, 128]``.
+    """
+    load_torch_ops().cache_write(k_new, v_new, slots, float(k_scale), float(v_scale), k_cache, v_cache)
+    return k_cache, v_cache
+
+
+def token_slots(btable, reqs, positions, page_size):
+    """Physical slot ``btable[req, pos // P] * P + pos % P`` of each (request,
+    position) pair, as int64 -- the ``slots`` argument of
+    ``qsa_cache_write`` for tokens appended at logical positions (the rule the
+    decode reads them back with, sm89_torch.py:31-44)."""
+    reqs = reqs.to(torch.long)
+    positions = positions.to(torch.long)
+    return btable.to(torch.long)[reqs, positions // page_size] * page_size + positions % page_size
+
+
 def chunk_tokens(num_q_heads, num_kv_heads) -> int:
     """Top-K entries one work item covers: 512 for GQA groups up to 8, 256
     for larger groups (their score tiles fill more tensor memory)."""
