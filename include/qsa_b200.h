@@ -194,9 +194,10 @@ typedef struct qsa_b200_cache_write_args {
 } qsa_b200_cache_write_args;
 
 /* Quantises new keys and values into the paged FP8 caches:
- *   cache[slot, g, d] = e4m3fn(x[t, g, d] / scale)   for slot = slots[t]
- * with x / scale an IEEE fp32 division and the conversion rounding to the
- * nearest E4M3FN value (ties to even), saturating at +-448: a finite value
+ *   cache[slot, g, d] = e4m3fn(x[t, g, d] * inv)   for slot = slots[t]
+ * with inv = 1 / scale rounded to fp32 once, an fp32 product, and the
+ * conversion rounding to the nearest E4M3FN value (ties to even), saturating
+ * at +-448: a finite value
  * beyond the range and an infinity become +-448, NaN stays NaN (torch's cast
  * turns |x| >= 464 into NaN instead). Rows of skipped tokens are left as they
  * were. Two tokens with the same slot race (the caller gives each slot once).

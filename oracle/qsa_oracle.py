@@ -126,7 +126,8 @@ def cache_write(k_cache, v_cache, k_new, v_new, slots, k_scale, v_scale):
     The reference fills its caches with ``(randn * 0.1).to(float8_e4m3fn)``
     in the ``[num_pages, P, Hkv, 128]`` layout and dequantises them as
     ``value * scale`` (sm89_cutedsl.py:48-62, :79; sm89_torch.py:43-44). The
-    writer stores ``e4m3fn(x / scale)``: an IEEE float32 division, then
+    writer stores ``e4m3fn(x * inv)`` with ``inv = float32(1 / scale)`` (an
+    IEEE float32 division, once) and a float32 product, then
     :func:`f32_to_e4m3fn_sat` (nearest, ties to even, saturating at +-448,
     NaN kept). ``k_cache``/``v_cache`` are uint8 byte arrays, ``k_new``/
     ``v_new`` float32 ``[tokens, Hkv, 128]`` (bf16 / fp16 inputs converted
@@ -138,8 +139,10 @@ def cache_write(k_cache, v_cache, k_new, v_new, slots, k_scale, v_scale):
     npages, page, hkv, d = kc.shape
     s = np.asarray(slots, dtype=np.int64)
     ok = (s >= 0) & (s < npages * page)
-    kq = f32_to_e4m3fn_sat(np.asarray(k_new, dtype=np.float32)[ok] / np.float32(k_scale))
-    vq = f32_to_e4m3fn_sat(np.asarray(v_new, dtype=np.float32)[ok] / np.float32(v_scale))
+    k_inv = np.float32(1.0) / np.float32(k_scale)
+    v_inv = np.float32(1.0) / np.float32(v_scale)
+    kq = f32_to_e4m3fn_sat(np.asarray(k_new, dtype=np.float32)[ok] * k_inv)
+    vq = f32_to_e4m3fn_sat(np.asarray(v_new, dtype=np.float32)[ok] * v_inv)
     kc.reshape(npages * page, hkv, d)[s[ok]] = kq
     vc.reshape(npages * page, hkv, d)[s[ok]] = vq
     return kc, vc

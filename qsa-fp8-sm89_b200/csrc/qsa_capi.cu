@@ -309,8 +309,9 @@ int qsa_b200_cache_write(const qsa_b200_cache_write_args* a, qsa_b200_stream_t s
   p.slots = a->slots;
   p.k_cache = static_cast<uint8_t*>(a->k_cache);
   p.v_cache = static_cast<uint8_t*>(a->v_cache);
-  p.k_scale = a->k_scale;
-  p.v_scale = a->v_scale;
+  // one fp32 reciprocal per call; every element is then multiplied by it
+  p.k_inv_scale = 1.0f / a->k_scale;
+  p.v_inv_scale = 1.0f / a->v_scale;
   p.tokens = a->tokens;
   p.num_kv_heads = a->num_kv_heads;
   p.page_size = a->page_size;

@@ -73,7 +73,7 @@ struct CacheWriteParams {
   const int64_t* slots;  // [tokens] physical token slots; outside [0, num_pages * P) = skipped
   uint8_t* k_cache;      // [num_pages, P, Hkv, 128] e4m3fn
   uint8_t* v_cache;
-  float k_scale, v_scale;
+  float k_inv_scale, v_inv_scale;  // 1 / scale, rounded to fp32
   int tokens;
   int num_kv_heads;
   int page_size;

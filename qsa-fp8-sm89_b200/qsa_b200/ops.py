@@ -115,14 +115,15 @@ def slots(indices, btable, t2r, page_size, num_pages, counts=None, *, count_colu
 
 def qsa_cache_write(k_new, v_new, slots, k_scale, v_scale, k_cache, v_cache):
     """Writes new keys and values into the paged FP8 caches the decode reads:
-    ``cache[slot, g, :] = e4m3fn(x[t, g, :] / scale)`` for ``slot =
+    ``cache[slot, g, :] = e4m3fn(x[t, g, :] * (1 / scale))`` for ``slot =
     slots[t]`` (``phys_page * P + offset``), in place, asynchronous on the
     current stream.
 
     The layout and the scale convention are the reference's cache producer
     (sm89_cutedsl.py:48-62: ``[num_pages, P, Hkv, 128]`` E4M3FN, dequantised
-    as ``value * scale``). The quotient is an IEEE fp32 division, rounded to
-    the nearest E4M3FN value (ties to even) and saturated at +-448: a finite
+    as ``value * scale``). ``1 / scale`` is rounded to fp32 once and each
+    product is an fp32 product, rounded to the nearest E4M3FN value (ties
+    to even) and saturated at +-448: a finite
     value beyond the range or an infinity becomes +-448 and NaN stays NaN,
     where ``torch``'s cast gives NaN for ``|x| >= 464``. Negative slots and
     slots past the cache are skipped.
