@@ -1,7 +1,7 @@
 """Benchmark of the sparse paged GQA FP8 decode path (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config 1] [--kernel auto|tc|simt]
+                    [--config 1] [--kernel auto|tc|simt] [--op decode|cache_write]
 
 Workload: BASELINE's headline shape, configs[1] (256 requests x 32q/8kv heads x
 d128, page 16, 32 pages/request, Top-K 512 = every token in random order) on
@@ -19,6 +19,10 @@ gate, Top-K indices, block table, request map) copied from pinned host memory
 and the output copied back inside the timed region; the K/V cache stays
 resident (it is the cache). ``--impl reference`` times the reference's eager
 path (a port of sm89_torch.torch_eager) on the host CPU instead.
+
+``--op cache_write`` (one GPU) times the paged cache writer instead: the
+whole configs[1] cache (256 requests x 512 tokens x 8 KV heads) written from
+bf16 keys and values at the block table's slots, GB/s of bytes moved.
 """
 
 from __future__ import annotations
@@ -44,7 +48,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch on
 # the bench workload, from the ncu capture summarised in profiles/ (None until
 # captured for the current kernel).
-NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): 278_276_864}
+NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): 278_276_864, ("cache write", 1): 772_670_000}
 
 
 def parse():
@@ -56,6 +60,7 @@ def parse():
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--kernel", default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=["decode", "cache_write"], default="decode")
     return ap.parse_args()
 
 
@@ -389,10 +394,78 @@ def run_ours(args):
     return 0
 
 
+# ------------------------------------------------------------ cache writer --
+def run_cache_write(args):
+    """One step = one qsa_cache_write of the whole configs[1] cache from bf16
+    keys and values (inputs resident in HBM, L2 flushed between steps)."""
+    import torch
+
+    if args.gpus != 1:
+        raise SystemExit("--op cache_write runs on one GPU")
+    dev = torch.device("cuda", 0)
+    import qsa_b200
+    from qsa_b200.inputs import CONFIGS
+
+    cfg = CONFIGS[args.config]
+    rows, hkv, page, ppr = cfg["rows"], cfg["hkv"], cfg["page"], cfg["ppr"]
+    tokens = rows * ppr * page
+    npages = rows * ppr
+    gen = torch.Generator(device=dev).manual_seed(0)
+    btable = torch.randperm(npages, generator=gen, device=dev).view(rows, ppr).to(torch.int32)
+    reqs = torch.arange(rows, device=dev).repeat_interleave(ppr * page)
+    pos = torch.arange(ppr * page, device=dev).repeat(rows)
+    slots = qsa_b200.token_slots(btable, reqs, pos, page)
+    k_new = torch.randn(tokens, hkv, 128, generator=gen, device=dev).to(torch.bfloat16)
+    v_new = torch.randn(tokens, hkv, 128, generator=gen, device=dev).to(torch.bfloat16)
+    kc = torch.empty(npages, page, hkv, 128, dtype=torch.float8_e4m3fn, device=dev)
+    vc = torch.empty_like(kc)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def call():
+        qsa_b200.qsa_cache_write(k_new, v_new, slots, 0.05, 0.05, kc, vc)
+
+    for _ in range(max(3, args.warmup)):
+        call()
+        flush.zero_()
+    stream = torch.cuda.current_stream()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        for i in range(args.steps):
+            starts[i].record(stream)
+            call()
+            ends[i].record(stream)
+            flush.zero_()
+        torch.cuda.synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    moved = tokens * hkv * 128 * (2 * 2 + 2 * 1) + tokens * 8  # bf16 K+V in, e4m3 K+V out, int64 slots
+    gbs = moved / (ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    line = {
+        "metric": "paged FP8 cache write GB/s (bf16 K/V -> e4m3fn, configs[1] cache)", "value": gbs,
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, e4m3fn out",
+        "data": "synthetic",
+        "config": {"workload": f"cache write of {workload_name(args.config)}", "tokens": tokens, "hkv": hkv,
+                   "page": page, "l2": "flushed between timed steps (256 MiB write, outside the timed events)"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "peak_source": peak_kind, "traffic": NCU_TRAFFIC_BYTES.get(("cache write", args.config)),
+                     "kernel": "qsa_cache_write_kernel",
+                     "bytes_per_step": moved},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.op == "cache_write":
+        return run_cache_write(args)
     return run_ours(args)
 
 
