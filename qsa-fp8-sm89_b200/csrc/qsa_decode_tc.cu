@@ -91,11 +91,12 @@ __host__ __device__ constexpr int pow2_at_least(int x) {
 
 template <int G>
 struct Cfg {
-  // softmax / epilogue warps: one per TMEM lane quadrant, or two (each taking
-  // half of the score tiles and half of the heads) where G >= 8 makes the
-  // per-item softmax longer than the item's K/V transfer. 12 warps leave up to
-  // 168 registers a thread, 16 warps 128 (one CTA per SM; an SM sub-partition
-  // has 16K registers and holds a quarter of the warps).
+  // softmax / epilogue warps: one set of four (one warp per TMEM lane
+  // quadrant), or two sets where G >= 8 makes one set's per-item softmax
+  // longer than the item's K/V transfer; each set takes half of the heads
+  // over all score tiles and runs independently of the other. 12 warps leave
+  // up to 168 registers a thread, 16 warps 128 (one CTA per SM; an SM
+  // sub-partition has 16K registers and holds a quarter of the warps).
   static constexpr int kSoftmaxWarps = G >= 8 ? 8 : 4;
   static constexpr int kSoftmaxSets = kSoftmaxWarps / 4;
   static constexpr int kThreads = 32 * (kSoftmax0 + kSoftmaxWarps);
@@ -108,9 +109,13 @@ struct Cfg {
   static constexpr int kTmemCols = pow2_at_least(kTmemBufs * kBufCols);
   static constexpr int kQsBytes = NS * 128;
   static_assert(kTiles * NS == 64 && (NO == 16 || NO == 32 || NO == 64), "TMEM load widths");
-  static constexpr int kHalfTiles = kTiles / kSoftmaxSets;                    // score tiles per softmax warp
-  static constexpr int kHalfHeads = G >= kSoftmaxSets ? G / kSoftmaxSets : 1;  // epilogue heads per softmax warp
-  static constexpr int kHeadCols = kHalfHeads * kTermsP;                       // O columns one softmax warp loads
+  static constexpr int kHalfHeads = G / kSoftmaxSets;    // heads of one softmax set
+  static constexpr int kHeadCols = kHalfHeads * kTermsP;  // O columns one softmax warp loads
+  // score columns of one set's heads in one tile, and the stride between
+  // tiles in the warp's score registers
+  static constexpr int kSetCols = kHalfHeads * kTermsQ;
+  static constexpr int kRawStride = kSoftmaxSets == 1 ? NS : kSetCols;
+  static_assert(kSoftmaxSets == 1 || kTiles * kSetCols == 32, "two-set score loads: 4 x 8 or 2 x 16 columns");
   static constexpr int kPsBytes = kTiles * NO * 128;
   // shared memory layout (offsets from a 1024-byte aligned base); every
   // region starts on a 128-byte boundary, the MMA operands on 1024
@@ -305,14 +310,14 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     }
     for (int m = 0; m < kMeta; ++m) {
       mbar_init(meta_full + m, 1);
-      mbar_init(meta_empty + m, kLoaders + 2);
+      mbar_init(meta_empty + m, kLoaders + 1 + C::kSoftmaxSets);
     }
     for (int b = 0; b < kTmemBufs; ++b) {
       mbar_init(s_full + b, 1);
       mbar_init(o_full + b, 1);
       mbar_init(tmem_empty + b, 32 * C::kSoftmaxWarps);
     }
-    for (int b = 0; b < 2; ++b) mbar_init(p_full + b, 1);
+    for (int b = 0; b < 2; ++b) mbar_init(p_full + b, C::kSoftmaxSets);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -591,16 +596,16 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     // Software pipelined: the softmax of item k runs before the epilogue of
     // item k-1, whose O accumulation has finished meanwhile. With two sets of
     // softmax warps, warps sw and sw + 4 share a TMEM lane quadrant and `half`
-    // picks their score tiles and epilogue heads (it only offsets addresses:
-    // every register array is indexed by compile-time constants).
+    // picks their heads (it only offsets addresses: every register array is
+    // indexed by compile-time constants); each set reduces over its own four
+    // warps with its own named barrier.
     const int q4 = warp & 3;                // TMEM lane quadrant of this warp
     const int sw = warp - kSoftmax0;        // 0 .. C::kSoftmaxWarps-1
     const int half = C::kSoftmaxSets > 1 ? (sw >> 2) : 0;  // softmax set
     const int tk = q4 * 32 + lane;          // token within a tile / head dim in the epilogue
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    const int j0 = half * C::kHalfTiles;    // first score tile of this warp
-    const int h0 = half * C::kHalfHeads;    // first epilogue head of this warp
-    const bool has_heads = h0 < G;          // false only for the second half when G == 1
+    const int h0 = half * C::kHalfHeads;    // first head of this warp's set
+    const int set_bar = 1 + half;           // named barrier of the set
     // state of the item whose epilogue is pending
     int e_k = -1, e_row = 0, e_g = 0, e_chunk = 0;
     bool e_any = false;  // the pending item has a valid tile
@@ -614,11 +619,9 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       tc_fence_after();
       // the O columns of this warp's heads (their kTermsP terms each)
       float v[C::kHeadCols];
-      if (has_heads)
-        tmem_ld_wait<C::kHeadCols>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + h0 * kTermsP, v);
+      tmem_ld_wait<C::kHeadCols>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + h0 * kTermsP, v);
       tc_fence_before();
       mbar_arrive(tmem_empty + tb);
-      if (!has_heads) return;
 #pragma unroll
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
         const int h = h0 + hh;
@@ -643,7 +646,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       const Item w = item_of(p, item_at(k));
       // the gate of this warp's heads, needed by the epilogue one iteration later
       __nv_bfloat16 gate[C::kHalfHeads];
-      if (p.num_chunks == 1 && has_heads) {
+      if (p.num_chunks == 1) {
 #pragma unroll
         for (int hh = 0; hh < C::kHalfHeads; ++hh)
           gate[hh] = p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h0 + hh) * kHeadDim + tk];
@@ -658,75 +661,84 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       }
       tc_fence_after();
       const uint32_t mask = tile_mask(m);
-      float qi[G];
+      constexpr int kSH = C::kHalfHeads;
+      float qi[kSH];
 #pragma unroll
-      for (int h = 0; h < G; ++h) qi[h] = qinv[m * G + h];
-      // this warp's score tiles: kHalfTiles * NS consecutive columns
-      float raw[C::kHalfTiles * C::NS];
-      if (!failed) tmem_ld_wait<C::kHalfTiles * C::NS>(tmem + lane_base + tb * C::kBufCols + j0 * C::NS, raw);
-      float sc[C::kHalfTiles][G];
+      for (int hh = 0; hh < kSH; ++hh) qi[hh] = qinv[m * G + h0 + hh];
+      // this set's score columns of every tile: (tile j, head hh, term t) at
+      // raw[j * kRawStride + hh * kTermsQ + t]
+      float raw[C::kTiles * C::kRawStride];
+      if (!failed) {
+        const uint32_t s0 = tmem + lane_base + tb * C::kBufCols + h0 * kTermsQ;
+        if constexpr (C::kSoftmaxSets == 1)
+          tmem_ld_wait<C::kTiles * C::NS>(s0, raw);
+        else if constexpr (C::kTiles == 4)
+          tmem_ld_4x8_wait(s0, C::NS, raw);
+        else
+          tmem_ld_2x16_wait(s0, C::NS, raw);
+      }
+      float sc[C::kTiles][kSH];
 #pragma unroll
-      for (int jj = 0; jj < C::kHalfTiles; ++jj) {
-        const int j = j0 + jj;
+      for (int j = 0; j < C::kTiles; ++j) {
         const bool ok = !failed && ((mask >> j) & 1u) && rowtab[m * C::kChunk + j * kTile + tk] >= 0;
 #pragma unroll
-        for (int h = 0; h < G; ++h) sc[jj][h] = ok ? combine_q(&raw[jj * C::NS + h * kTermsQ]) * qi[h] : -INFINITY;
+        for (int hh = 0; hh < kSH; ++hh)
+          sc[j][hh] = ok ? combine_q(&raw[j * C::kRawStride + hh * kTermsQ]) * qi[hh] : -INFINITY;
       }
-      // exact max per head over the chunk (one partial maximum per softmax warp)
+      // exact max per head over the chunk (one partial maximum per warp of the set)
+      float* rmax = red_max + (pb * C::kSoftmaxWarps + half * 4) * G + h0;
+      float* rsum = red_sum + (pb * C::kSoftmaxWarps + half * 4) * G + h0;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float mx = sc[0][h];
+      for (int hh = 0; hh < kSH; ++hh) {
+        float mx = sc[0][hh];
 #pragma unroll
-        for (int jj = 1; jj < C::kHalfTiles; ++jj) mx = fmaxf(mx, sc[jj][h]);
+        for (int j = 1; j < C::kTiles; ++j) mx = fmaxf(mx, sc[j][hh]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) red_max[(pb * C::kSoftmaxWarps + sw) * G + h] = mx;
+        if (lane == 0) rmax[q4 * G + hh] = mx;
       }
-      named_bar_sync(1, 32 * C::kSoftmaxWarps);
-      if (sw == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // row table and scales read
-      float m_h[G];
+      named_bar_sync(set_bar, 128);
+      if (q4 == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // row table and scales read
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float* rm = red_max + pb * C::kSoftmaxWarps * G + h;
-        float mx = rm[0];
+      for (int hh = 0; hh < kSH; ++hh) {
+        float mx = rmax[hh];
 #pragma unroll
-        for (int i = 1; i < C::kSoftmaxWarps; ++i) mx = fmaxf(mx, rm[i * G]);
-        m_h[h] = mx;
+        for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * G + hh]);
         float sum = 0.f;
 #pragma unroll
-        for (int jj = 0; jj < C::kHalfTiles; ++jj) {
-          const float pr = sc[jj][h] == -INFINITY ? 0.f : exp2f(sc[jj][h] - mx);
-          sc[jj][h] = pr;
+        for (int j = 0; j < C::kTiles; ++j) {
+          const float pr = sc[j][hh] == -INFINITY ? 0.f : exp2f(sc[j][hh] - mx);
+          sc[j][hh] = pr;
           sum += pr;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) red_sum[(pb * C::kSoftmaxWarps + sw) * G + h] = sum;
+        if (lane == 0) rsum[q4 * G + hh] = sum;
       }
-      // probabilities -> FP8 terms of p*256 (row h*kTermsP+j of Ps, one byte per
+      // probabilities -> FP8 terms of p*256 (row h*kTermsP+t of Ps, one byte per
       // token), two heads per conversion
       uint8_t* ps = smem + C::kPs + pb * C::kPsBytes;
 #pragma unroll
-      for (int jj = 0; jj < C::kHalfTiles; ++jj) {
-        const int j = j0 + jj;
+      for (int j = 0; j < C::kTiles; ++j) {
         if ((mask >> j) & 1u) {
           uint8_t* pt = ps + j * C::NO * 128;
 #pragma unroll
-          for (int h = 0; h < G; h += 2) {
+          for (int hh = 0; hh < kSH; hh += 2) {
             uint16_t tt[kTermsP];
-            split_p2(sc[jj][h] * 256.0f, h + 1 < G ? sc[jj][h + 1] * 256.0f : 0.f, tt);
+            split_p2(sc[j][hh] * 256.0f, hh + 1 < kSH ? sc[j][hh + 1] * 256.0f : 0.f, tt);
 #pragma unroll
             for (int t = 0; t < kTermsP; ++t) {
-              pt[sw128_offset(h * kTermsP + t, tk)] = (uint8_t)(tt[t] & 0xffu);
-              if (h + 1 < G) pt[sw128_offset((h + 1) * kTermsP + t, tk)] = (uint8_t)(tt[t] >> 8);
+              pt[sw128_offset((h0 + hh) * kTermsP + t, tk)] = (uint8_t)(tt[t] & 0xffu);
+              if (hh + 1 < kSH) pt[sw128_offset((h0 + hh + 1) * kTermsP + t, tk)] = (uint8_t)(tt[t] >> 8);
             }
           }
-          for (int r = G * kTermsP; r < C::NO; ++r) pt[sw128_offset(r, tk)] = 0;
+          if (half == 0)
+            for (int r = G * kTermsP; r < C::NO; ++r) pt[sw128_offset(r, tk)] = 0;
         }
       }
       fence_proxy_async_smem();
-      named_bar_sync(1, 32 * C::kSoftmaxWarps);
-      if (sw == 0 && lane == 0 && !failed) mbar_arrive(p_full + pb);
+      named_bar_sync(set_bar, 128);
+      if (q4 == 0 && lane == 0 && !failed) mbar_arrive(p_full + pb);
 
       // ---- epilogue of the previous item, then this item becomes pending ---
       if (e_k >= 0) epilogue();
@@ -739,18 +751,17 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
         // this warp's heads, read back from the group's partials (a head index
         // that is not a compile-time constant must not index a register array)
-        const int h = min(h0 + hh, G - 1);
-        const float* rs = red_sum + pb * C::kSoftmaxWarps * G + h;
-        const float* rm = red_max + pb * C::kSoftmaxWarps * G + h;
+        const float* rs = red_sum + (pb * C::kSoftmaxWarps + half * 4) * G + h0 + hh;
+        const float* rm = red_max + (pb * C::kSoftmaxWarps + half * 4) * G + h0 + hh;
         float l = 0.f, mx = rm[0];
 #pragma unroll
-        for (int i = 0; i < C::kSoftmaxWarps; ++i) {
+        for (int i = 0; i < 4; ++i) {
           l += rs[i * G];
           mx = fmaxf(mx, rm[i * G]);
         }
         e_m[hh] = mx;
         e_l[hh] = l;
-        e_gate[hh] = (p.num_chunks == 1 && has_heads) ? gate[hh] : __float2bfloat16_rn(0.f);
+        e_gate[hh] = p.num_chunks == 1 ? gate[hh] : __float2bfloat16_rn(0.f);
       }
     }
     if (e_k >= 0) epilogue();
