@@ -141,28 +141,49 @@ __global__ void qsa_decode_simt_kernel(DecodeParams p) {
 
 // Merge the per-chunk partial results of one (row, query head): the
 // flash-decoding combine, in the log2 domain of the kernels' softmax.
-__global__ void qsa_combine_kernel(DecodeParams p) {
-  const int h = blockIdx.x % p.num_q_heads;
-  const int row = blockIdx.x / p.num_q_heads;
-  const int d = threadIdx.x;
-  const int64_t base = ((int64_t)row * p.num_q_heads + h) * p.num_chunks;
+// One warp per (row, query head), lane l owning dims 4l .. 4l+3: the chunk
+// partials merge by their log2-sum-exp2 weights (flash-decoding), then the
+// gate and v_scale. Every chunk's partial loads leave before the first
+// weighted sum, so the kernel streams at HBM rate.
+constexpr int kCombineWarps = 8;
+__global__ void __launch_bounds__(32 * kCombineWarps) qsa_combine_kernel(DecodeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t hr = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);  // row * Hq + head
+  if (hr >= (int64_t)p.rows * p.num_q_heads) return;
+  const int64_t base = hr * p.num_chunks;
+  const float* lse = p.part_lse + base;
+  const float4* po = reinterpret_cast<const float4*>(p.part_o + base * kHeadDim) + lane;
   float mx = -INFINITY;
-  for (int c = 0; c < p.num_chunks; ++c) mx = fmaxf(mx, p.part_lse[base + c]);
-  float o = 0.f;
+  for (int c = 0; c < p.num_chunks; ++c) mx = fmaxf(mx, __ldg(lse + c));
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float wsum = 0.f;
   if (mx != -INFINITY) {
-    float wsum = 0.f;
+#pragma unroll 4
     for (int c = 0; c < p.num_chunks; ++c) {
-      const float lse = p.part_lse[base + c];
-      if (lse == -INFINITY) continue;
-      const float w = exp2f(lse - mx);
+      const float l = __ldg(lse + c);
+      const float4 v = __ldg(po + c * (kHeadDim / 4));
+      const float w = l == -INFINITY ? 0.f : exp2f(l - mx);
       wsum += w;
-      o = fmaf(w, p.part_o[(base + c) * kHeadDim + d], o);
+      acc.x = fmaf(w, v.x, acc.x);
+      acc.y = fmaf(w, v.y, acc.y);
+      acc.z = fmaf(w, v.z, acc.z);
+      acc.w = fmaf(w, v.w, acc.w);
     }
-    o = o / wsum;
+    const float inv = 1.0f / wsum;
+    acc.x *= inv, acc.y *= inv, acc.z *= inv, acc.w *= inv;
   }
-  const int64_t off = ((int64_t)row * p.num_q_heads + h) * kHeadDim + d;
-  const float gt = __bfloat162float(p.gate[off]);
-  p.out[off] = __float2bfloat16_rn(o * p.v_scale * sigmoidf_(gt));
+  const int64_t off = hr * kHeadDim + lane * 4;
+  const uint2 gu = __ldg(reinterpret_cast<const uint2*>(p.gate + off));
+  const float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gu.x));
+  const float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gu.y));
+  const __nv_bfloat162 o01 = __floats2bfloat162_rn(acc.x * p.v_scale * sigmoidf_(g01.x),
+                                                   acc.y * p.v_scale * sigmoidf_(g01.y));
+  const __nv_bfloat162 o23 = __floats2bfloat162_rn(acc.z * p.v_scale * sigmoidf_(g23.x),
+                                                   acc.w * p.v_scale * sigmoidf_(g23.y));
+  uint2 ou;
+  ou.x = *reinterpret_cast<const uint32_t*>(&o01);
+  ou.y = *reinterpret_cast<const uint32_t*>(&o23);
+  *reinterpret_cast<uint2*>(p.out + off) = ou;
 }
 
 // Physical slot of every Top-K entry (-1 where masked): the bit-exact view of
@@ -187,7 +208,8 @@ cudaError_t launch_decode_simt(const DecodeParams& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream) {
-  qsa_combine_kernel<<<(unsigned)(p.rows * p.num_q_heads), kHeadDim, 0, stream>>>(p);
+  const int64_t warps = (int64_t)p.rows * p.num_q_heads;
+  qsa_combine_kernel<<<(unsigned)((warps + kCombineWarps - 1) / kCombineWarps), 32 * kCombineWarps, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
