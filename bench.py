@@ -81,6 +81,45 @@ def workload_name(cfg: int) -> str:
 
 
 # ------------------------------------------------------------------ clocks --
+def nvml_handle(index: int):
+    """NVML handle of CUDA device ``index``, matched by PCI bus id (NVML's
+    own index order need not follow CUDA's), or None without NVML."""
+    try:
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(index)
+        bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+        try:
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(index)
+    except Exception:
+        return None
+
+
+def bind_local_cpus(index: int) -> bool:
+    """Restricts this process to the CPUs NVML reports as local to CUDA
+    device ``index`` (read through nvmlDeviceGetCpuAffinity; nothing on the
+    GPU changes), so that its pinned host buffers sit on the GPU's NUMA node."""
+    h = nvml_handle(index)
+    if h is None:
+        return False
+    try:
+        import pynvml
+
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+        cpus = {w * 64 + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+        cpus &= set(range(os.cpu_count() or 0))
+        if not cpus:
+            return False
+        os.sched_setaffinity(0, cpus)
+        return True
+    except Exception:
+        return False
+
+
 class ClockSampler:
     """Samples SM clock and clock-event reasons through NVML every few ms."""
 
@@ -97,9 +136,8 @@ class ClockSampler:
         try:
             import pynvml
 
-            pynvml.nvmlInit()
             self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.h = nvml_handle(index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
             self.ok = True
         except Exception:
@@ -198,7 +236,7 @@ def cpu_eager_sample(w, rows: int, calls: int, warmup: int):
 
     from oracle.eager_port import torch_eager_port
 
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     torch.set_num_threads(threads)
     sel = torch.arange(rows, device=w.btable.device)
     bt = w.btable[w.t2r[sel].long()].long()
@@ -268,6 +306,8 @@ def run_ours(args):
     rank, local, world = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    all_cpus = os.sched_getaffinity(0)
+    numa_bound = bind_local_cpus(local)
     import qsa_b200
     from qsa_b200 import capi
     from qsa_b200.inputs import kv_bytes, make_workload
@@ -374,6 +414,7 @@ def run_ours(args):
     # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        os.sched_setaffinity(0, all_cpus)  # the CPU baseline gets every core again
         times, ukv, threads = cpu_eager_sample(w, 32, 5, 3)
         med = statistics.median(times)
         cpu = {"value": ukv / med / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
@@ -409,7 +450,8 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms,
                     "method": "3-stream pipeline: step i's host->device inputs and device->host output overlap "
-                              "the decode of step i-1; all steps' copies inside the timed region"},
+                              "the decode of step i-1; all steps' copies inside the timed region",
+                    "host_cpus_bound_to_gpu_numa_node": numa_bound},
             "gpu_launches": launches_per_call * args.steps,
             "clocks": clocks,
             "device_error": dev_err,
