@@ -309,7 +309,7 @@ def run_ours(args):
     all_cpus = os.sched_getaffinity(0)
     numa_bound = bind_local_cpus(local)
     import qsa_b200
-    from qsa_b200 import capi
+    from qsa_b200 import capi, ops
     from qsa_b200.inputs import kv_bytes, make_workload
 
     w = make_workload(args.config, dev, seed=0, shard=rank)
@@ -321,7 +321,7 @@ def run_ours(args):
     # combine for Top-K rows longer than one chunk); CUDA-core path: the decode
     # kernel (+ combine)
     chunk = 512 if w.meta["hq"] // w.meta["hkv"] <= 8 else 256
-    tc_path = kernel == "tc" or (kernel == "auto" and w.meta["hq"] // w.meta["hkv"] in (1, 2, 4, 8, 16))
+    tc_path = kernel == "tc" or (kernel == "auto" and ops.tc_supports_group(w.meta["hq"] // w.meta["hkv"]))
     launches_per_call = (2 if tc_path else 1) + (1 if w.meta["topk"] > chunk else 0)
 
     def call():

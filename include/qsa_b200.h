@@ -65,7 +65,8 @@ enum {
 };
 
 /* Kernel selection. AUTO picks the tensor-core kernel for group sizes
- * 1, 2, 4, 8, 16 and the CUDA-core kernel for the others. */
+ * (Hq / Hkv) 1 to 8 and 10, 12, 14, 16, and the CUDA-core kernel for the
+ * others (up to 32). */
 enum { QSA_B200_KERNEL_AUTO = 0, QSA_B200_KERNEL_TC = 1, QSA_B200_KERNEL_SIMT = 2 };
 
 typedef struct qsa_b200_decode_args {

@@ -1,7 +1,7 @@
 // C ABI of libqsa_b200.so (declared in include/qsa_b200.h).
 //
 // Validates arguments, turns them into qsa::DecodeParams and launches the
-// decode (the tensor-core kernel for group sizes 1/2/4/8/16, otherwise the
+// decode (the tensor-core kernel for group sizes 1-8, 10, 12, 14, 16, otherwise the
 // CUDA-core kernel), plus the split combine when a Top-K row is longer than
 // one chunk. Workspace layout (each part 256-byte aligned): the row map and
 // the tile flags (tensor-core kernel only), the partial outputs and the

@@ -1,7 +1,7 @@
 // General-shape decode kernel (CUDA cores), plus the slot and combine kernels.
 //
 // qsa_decode_simt_kernel covers every GQA group size (the tensor-core kernel
-// in qsa_decode_tc.cu handles group sizes 1, 2, 4, 8 and 16). One CTA serves
+// in qsa_decode_tc.cu handles group sizes 1-8, 10, 12, 14 and 16). One CTA serves
 // one (row, KV head, chunk) with one warp per query head of the group; lane l
 // owns dims 4l..4l+3. Tokens go in 32-token tiles: lane j decodes token j of
 // the tile, every lane forms its 4-dim partial dot product for all 32 tokens

@@ -94,10 +94,14 @@ struct Cfg {
   // softmax / epilogue warps: one set of four (one warp per TMEM lane
   // quadrant), or two sets where G >= 8 makes one set's per-item softmax
   // longer than the item's K/V transfer; each set takes half of the heads
-  // over all score tiles and runs independently of the other. 12 warps leave
-  // up to 168 registers a thread, 16 warps 128 (one CTA per SM; an SM
-  // sub-partition has 16K registers and holds a quarter of the warps).
-  static constexpr int kSoftmaxWarps = G >= 8 ? 8 : 4;
+  // (so two sets only for even G) over all score tiles and runs independently
+  // of the other. 12 warps leave up to 168 registers a thread, 16 warps 128
+  // (one CTA per SM; an SM sub-partition has 16K registers and holds a
+  // quarter of the warps).
+  // GP: the heads the softmax handles -- an odd G from 5 up gets one padding
+  // head (zero query rows, never written out) so that two sets split it
+  static constexpr int GP = (G >= 5 && G % 2 == 1) ? G + 1 : G;
+  static constexpr int kSoftmaxWarps = (GP >= 6 && GP % 2 == 0) ? 8 : 4;
   static constexpr int kSoftmaxSets = kSoftmaxWarps / 4;
   static constexpr int kThreads = 32 * (kSoftmax0 + kSoftmaxWarps);
   static_assert(kThreads % 128 == 0, "whole warpgroups, so the four sub-partitions hold equal shares");
@@ -108,14 +112,19 @@ struct Cfg {
   static constexpr int kBufCols = (kTiles * NS + NO + 31) / 32 * 32;  // S tiles + O, per TMEM buffer
   static constexpr int kTmemCols = pow2_at_least(kTmemBufs * kBufCols);
   static constexpr int kQsBytes = NS * 128;
-  static_assert(kTiles * NS == 64 && (NO == 16 || NO == 32 || NO == 64), "TMEM load widths");
-  static constexpr int kHalfHeads = G / kSoftmaxSets;    // heads of one softmax set
-  static constexpr int kHeadCols = kHalfHeads * kTermsP;  // O columns one softmax warp loads
+  static_assert(kTiles * NS == 64 && NO % 16 == 0 && NO <= 64, "TMEM budget and MMA N");
+  static_assert(GP * kTermsQ <= NS && GP * kTermsP <= NO, "a padding head fits the S and O columns");
+  static constexpr int kHalfHeads = GP / kSoftmaxSets;   // heads of one softmax set
+  static constexpr int kHeadCols = kHalfHeads * kTermsP;  // O columns of one softmax warp's heads
+  // ... loaded as a supported tcgen05.ld width (the extra columns lie inside
+  // the TMEM buffer and are not used)
+  static constexpr int kHeadColsLd = kHeadCols <= 4 ? 4 : kHeadCols <= 8 ? 8 : kHeadCols <= 16 ? 16
+                                                                          : kHeadCols <= 32 ? 32 : 64;
   // score columns of one set's heads in one tile, and the stride between
   // tiles in the warp's score registers
   static constexpr int kSetCols = kHalfHeads * kTermsQ;
-  static constexpr int kRawStride = kSoftmaxSets == 1 ? NS : kSetCols;
-  static_assert(kSoftmaxSets == 1 || kTiles * kSetCols == 32, "two-set score loads: 4 x 8 or 2 x 16 columns");
+  static constexpr int kRawStride = kSoftmaxSets == 1 ? NS : 32 / kTiles;  // 4 x 8 or 2 x 16 columns
+  static_assert(kSoftmaxSets == 1 || kSetCols <= kRawStride, "two-set score loads: 4 x 8 or 2 x 16 columns");
   static constexpr int kPsBytes = kTiles * NO * 128;
   // shared memory layout (offsets from a 1024-byte aligned base); every
   // region starts on a 128-byte boundary, the MMA operands on 1024
@@ -124,9 +133,9 @@ struct Cfg {
   static constexpr int kRowTab = kPs + 2 * kPsBytes;                   // int32 [kMeta][kChunk] token slots
   static constexpr int kTileFlags = kRowTab + kMeta * kChunk * 4;      // uint8 [kMeta][16] (kTiles used)
   static constexpr int kQinv = kTileFlags + kMeta * 16;                // float [kMeta][G]
-  static constexpr int kRedMax = align128(kQinv + kMeta * G * 4);      // float [2][kSoftmaxWarps][G]
-  static constexpr int kRedSum = align128(kRedMax + 2 * kSoftmaxWarps * G * 4);  // float [2][kSoftmaxWarps][G]
-  static constexpr int kBars = align128(kRedSum + 2 * kSoftmaxWarps * G * 4);
+  static constexpr int kRedMax = align128(kQinv + kMeta * G * 4);      // float [2][kSoftmaxWarps][GP]
+  static constexpr int kRedSum = align128(kRedMax + 2 * kSoftmaxWarps * GP * 4);  // float [2][kSoftmaxWarps][GP]
+  static constexpr int kBars = align128(kRedSum + 2 * kSoftmaxWarps * GP * 4);
   static constexpr int kMaxSlots = 16;
   static constexpr int kNumBars = 2 * kMaxSlots + 2 * kMeta + 3 * kTmemBufs + 2;
   // tmem address (+0), abort flag (+8), item ids of the metadata slots
@@ -618,8 +627,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       if (failed) return;
       tc_fence_after();
       // the O columns of this warp's heads (their kTermsP terms each)
-      float v[C::kHeadCols];
-      tmem_ld_wait<C::kHeadCols>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + h0 * kTermsP, v);
+      float v[C::kHeadColsLd];
+      tmem_ld_wait<C::kHeadColsLd>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + h0 * kTermsP, v);
       tc_fence_before();
       mbar_arrive(tmem_empty + tb);
 #pragma unroll
@@ -628,6 +637,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         const float o = (e_any && e_l[hh] > 0.f)
                             ? combine_p(v + hh * kTermsP) * (1.0f / 256.0f) / e_l[hh]
                             : 0.f;
+        if (h >= G) continue;  // the padding head of an odd group
         const int64_t hrow = (int64_t)e_row * p.num_q_heads + e_g * G + h;
         if (p.num_chunks == 1) {
           const float gt = __bfloat162float(e_gate[hh]);
@@ -649,7 +659,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       if (p.num_chunks == 1) {
 #pragma unroll
         for (int hh = 0; hh < C::kHalfHeads; ++hh)
-          gate[hh] = p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h0 + hh) * kHeadDim + tk];
+          gate[hh] = h0 + hh < G ? p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h0 + hh) * kHeadDim + tk]
+                                 : __float2bfloat16_rn(0.f);
       }
       // meta_full publishes the row table and query scales; s_full the
       // scores. Once anything failed the group keeps walking its items (the
@@ -664,7 +675,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       constexpr int kSH = C::kHalfHeads;
       float qi[kSH];
 #pragma unroll
-      for (int hh = 0; hh < kSH; ++hh) qi[hh] = qinv[m * G + h0 + hh];
+      for (int hh = 0; hh < kSH; ++hh) qi[hh] = h0 + hh < G ? qinv[m * G + h0 + hh] : 0.f;
       // this set's score columns of every tile: (tile j, head hh, term t) at
       // raw[j * kRawStride + hh * kTermsQ + t]
       float raw[C::kTiles * C::kRawStride];
@@ -686,8 +697,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
           sc[j][hh] = ok ? combine_q(&raw[j * C::kRawStride + hh * kTermsQ]) * qi[hh] : -INFINITY;
       }
       // exact max per head over the chunk (one partial maximum per warp of the set)
-      float* rmax = red_max + (pb * C::kSoftmaxWarps + half * 4) * G + h0;
-      float* rsum = red_sum + (pb * C::kSoftmaxWarps + half * 4) * G + h0;
+      float* rmax = red_max + (pb * C::kSoftmaxWarps + half * 4) * C::GP + h0;
+      float* rsum = red_sum + (pb * C::kSoftmaxWarps + half * 4) * C::GP + h0;
 #pragma unroll
       for (int hh = 0; hh < kSH; ++hh) {
         float mx = sc[0][hh];
@@ -695,7 +706,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         for (int j = 1; j < C::kTiles; ++j) mx = fmaxf(mx, sc[j][hh]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) rmax[q4 * G + hh] = mx;
+        if (lane == 0) rmax[q4 * C::GP + hh] = mx;
       }
       named_bar_sync(set_bar, 128);
       if (q4 == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // row table and scales read
@@ -703,7 +714,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       for (int hh = 0; hh < kSH; ++hh) {
         float mx = rmax[hh];
 #pragma unroll
-        for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * G + hh]);
+        for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * C::GP + hh]);
         float sum = 0.f;
 #pragma unroll
         for (int j = 0; j < C::kTiles; ++j) {
@@ -713,7 +724,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) rsum[q4 * G + hh] = sum;
+        if (lane == 0) rsum[q4 * C::GP + hh] = sum;
       }
       // probabilities -> FP8 terms of p*256 (row h*kTermsP+t of Ps, one byte per
       // token), two heads per conversion
@@ -733,7 +744,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
             }
           }
           if (half == 0)
-            for (int r = G * kTermsP; r < C::NO; ++r) pt[sw128_offset(r, tk)] = 0;
+            for (int r = C::GP * kTermsP; r < C::NO; ++r) pt[sw128_offset(r, tk)] = 0;
         }
       }
       fence_proxy_async_smem();
@@ -751,13 +762,13 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
         // this warp's heads, read back from the group's partials (a head index
         // that is not a compile-time constant must not index a register array)
-        const float* rs = red_sum + (pb * C::kSoftmaxWarps + half * 4) * G + h0 + hh;
-        const float* rm = red_max + (pb * C::kSoftmaxWarps + half * 4) * G + h0 + hh;
+        const float* rs = red_sum + (pb * C::kSoftmaxWarps + half * 4) * C::GP + h0 + hh;
+        const float* rm = red_max + (pb * C::kSoftmaxWarps + half * 4) * C::GP + h0 + hh;
         float l = 0.f, mx = rm[0];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          l += rs[i * G];
-          mx = fmaxf(mx, rm[i * G]);
+          l += rs[i * C::GP];
+          mx = fmaxf(mx, rm[i * C::GP]);
         }
         e_m[hh] = mx;
         e_l[hh] = l;
@@ -934,15 +945,22 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
 int tc_chunk_tokens(int group) { return group <= 8 ? 4 * kTile : 2 * kTile; }
 
 bool tc_supports_group(int group) {
-  return group == 1 || group == 2 || group == 4 || group == 8 || group == 16;
+  return (group >= 1 && group <= 8) || (group <= 16 && group % 2 == 0);
 }
 
 cudaError_t launch_decode_tc(const DecodeParams& p, cudaStream_t stream) {
   switch (p.group) {
     case 1: return launch_g<1>(p, stream);
     case 2: return launch_g<2>(p, stream);
+    case 3: return launch_g<3>(p, stream);
     case 4: return launch_g<4>(p, stream);
+    case 5: return launch_g<5>(p, stream);
+    case 6: return launch_g<6>(p, stream);
+    case 7: return launch_g<7>(p, stream);
     case 8: return launch_g<8>(p, stream);
+    case 10: return launch_g<10>(p, stream);
+    case 12: return launch_g<12>(p, stream);
+    case 14: return launch_g<14>(p, stream);
     case 16: return launch_g<16>(p, stream);
     default: return cudaErrorInvalidValue;
   }

@@ -149,6 +149,12 @@ def token_slots(btable, reqs, positions, page_size):
     return btable.to(torch.long)[reqs, positions // page_size] * page_size + positions % page_size
 
 
+def tc_supports_group(group: int) -> bool:
+    """Group sizes (Hq / Hkv) of the tensor-core kernel: 1 to 8 and the even
+    sizes up to 16 (the others run on the CUDA-core kernel)."""
+    return 1 <= group <= 8 or (group <= 16 and group % 2 == 0)
+
+
 def chunk_tokens(num_q_heads, num_kv_heads) -> int:
     """Top-K entries one work item covers: 512 for GQA groups up to 8, 256
     for larger groups (their score tiles fill more tensor memory)."""
@@ -165,7 +171,7 @@ def workspace_bytes(rows, num_q_heads, num_kv_heads, topk, kernel="auto") -> int
     c = chunk_tokens(num_q_heads, num_kv_heads)
     chunks = 1 if topk <= c else -(-topk // c)
     group = num_q_heads // num_kv_heads
-    tc = kernel == "tc" or (kernel == "auto" and group in (1, 2, 4, 8, 16))
+    tc = kernel == "tc" or (kernel == "auto" and tc_supports_group(group))
     total = a256(rows * chunks * c * 4) + a256(rows * chunks * 16) if (tc and rows > 0) else 0
     if chunks > 1:
         n = rows * num_q_heads * chunks

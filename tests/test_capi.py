@@ -81,7 +81,7 @@ def _args_cpu(**over):
     (dict(indices_stride=10), -2),
     (dict(btable_stride=2), -2),
     (dict(kernel=7), -3),
-    (dict(num_q_heads=24, kernel=1), -3),
+    (dict(num_q_heads=72, kernel=1), -3),  # G = 9: odd above 8 runs on the CUDA-core kernel only
 ])
 def test_validation_errors(over, code):
     from qsa_b200 import capi
@@ -133,9 +133,12 @@ def test_workspace_sizes():
     n = 4 * 128 * 5
     rowmap = 4 * 5 * 256 * 4 + 512
     assert capi.workspace_bytes(a) == rowmap + n * 512 + n * 4 == ops.workspace_bytes(4, 128, 8, 1100)
-    a.num_q_heads = 96  # group 12: CUDA-core kernel (256-entry chunks), no row map
+    a.num_q_heads = 96  # group 12: tensor-core kernel, 256-entry chunks
     n = 4 * 96 * 5
-    assert capi.workspace_bytes(a) == n * 512 + n * 4 == ops.workspace_bytes(4, 96, 8, 1100)
+    assert capi.workspace_bytes(a) == rowmap + n * 512 + n * 4 == ops.workspace_bytes(4, 96, 8, 1100)
+    a.num_q_heads = 72  # group 9: CUDA-core kernel (256-entry chunks), no row map
+    n = 4 * 72 * 5
+    assert capi.workspace_bytes(a) == n * 512 + -(-n * 4 // 256) * 256 == ops.workspace_bytes(4, 72, 8, 1100)
 
 
 def test_torch_ops_register_and_refuse_cpu_tensors():

@@ -180,7 +180,9 @@ def test_ragged_gqa8_split(kernel):
 # -------------------------------------------------------- shape coverage ----
 @pytest.mark.parametrize("hq,hkv,kernel", [
     (8, 8, "tc"), (16, 8, "tc"), (32, 8, "tc"), (64, 8, "tc"), (128, 8, "tc"),
-    (24, 8, "simt"), (48, 8, "simt"), (32, 8, "simt"), (32, 4, "tc"), (32, 1, "simt"),
+    (24, 8, "tc"), (40, 8, "tc"), (48, 8, "tc"), (56, 8, "tc"), (28, 4, "tc"),
+    (80, 8, "tc"), (96, 8, "tc"), (112, 8, "tc"),
+    (24, 8, "simt"), (48, 8, "simt"), (32, 8, "simt"), (32, 4, "tc"), (32, 1, "simt"), (72, 8, "auto"),
 ])
 def test_group_sizes(hq, hkv, kernel):
     from qsa_b200 import qsa_decode
@@ -191,6 +193,22 @@ def test_group_sizes(hq, hkv, kernel):
     torch.cuda.synchronize()
     ref = oracle_subset(w, list(range(6)))
     check_close(bits(out), ref, what=f"G={hq // hkv}/{kernel}")
+    assert max_ulps(bits(out), ref) <= 1.0
+
+
+@pytest.mark.parametrize("hq,hkv", [(24, 8), (56, 8), (96, 8), (112, 8)])
+def test_group_sizes_split(hq, hkv):
+    """Odd and padded group sizes on the tensor-core kernel with a Top-K long
+    enough to split into chunks (512 entries per chunk up to G = 8, 256
+    above)."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=hq * 3 + hkv, rows=4, hq=hq, hkv=hkv, ppr=64, topk=700, mode="sample")
+    out = qsa_decode(*w.args(), kernel="tc")
+    torch.cuda.synchronize()
+    ref = oracle_subset(w, list(range(4)))
+    check_close(bits(out), ref, what=f"G={hq // hkv}/split")
     assert max_ulps(bits(out), ref) <= 1.0
 
 
