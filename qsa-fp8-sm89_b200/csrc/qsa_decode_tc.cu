@@ -634,14 +634,19 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
 #pragma unroll
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
         const int h = h0 + hh;
+        // branch-free division and exponential (the intrinsics), so the
+        // heads' chains interleave; their few-ulp fp32 error is far below the
+        // bf16 rounding of the result
         const float o = (e_any && e_l[hh] > 0.f)
-                            ? combine_p(v + hh * kTermsP) * (1.0f / 256.0f) / e_l[hh]
+                            ? __fdividef(combine_p(v + hh * kTermsP) * (1.0f / 256.0f), e_l[hh])
                             : 0.f;
         if (h >= G) continue;  // the padding head of an odd group
         const int64_t hrow = (int64_t)e_row * p.num_q_heads + e_g * G + h;
         if (p.num_chunks == 1) {
           const float gt = __bfloat162float(e_gate[hh]);
-          p.out[hrow * kHeadDim + tk] = __float2bfloat16_rn(o * p.v_scale * (1.0f / (1.0f + expf(-gt))));
+          // exp(80) keeps 1 + e below 2^126, where the fast division is exact enough
+          const float sig = __fdividef(1.0f, 1.0f + __expf(fminf(-gt, 80.0f)));
+          p.out[hrow * kHeadDim + tk] = __float2bfloat16_rn(o * p.v_scale * sig);
         } else {
           const int64_t pidx = hrow * p.num_chunks + e_chunk;
           p.part_o[pidx * kHeadDim + tk] = o;
