@@ -203,6 +203,13 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+// Maximum over the warp's 32 lanes in one instruction (sm_100a); NaN inputs
+// are ignored, as fmaxf ignores them.
+__device__ __forceinline__ float warp_max(float x) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;\n" : "=f"(r) : "f"(x));
+  return r;
+}
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
@@ -378,8 +385,12 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q_c[h].y));
         const float x[4] = {a.x, a.y, c.x, c.y};
         float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+        if constexpr (G >= 8) {  // large groups: the decoder's per-item work shows
+          amax = warp_max(amax);
+        } else {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+          for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        }
         int e = 0;  // 2^e maps the head's largest |q| into [128, 256)
         if (amax > 0.f && amax <= 3.0e38f) {
           const int ex = (int)((__float_as_uint(amax) >> 23) & 0xff) - 127;
@@ -709,8 +720,15 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         float mx = sc[0][hh];
 #pragma unroll
         for (int j = 1; j < C::kTiles; ++j) mx = fmaxf(mx, sc[j][hh]);
+        // one redux for the large groups, whose softmax bounds the kernel; the
+        // shuffle tree has the shorter latency that the small groups' pipeline
+        // (softmax -> P -> O MMA -> ring slot) prefers
+        if constexpr (G >= 8) {
+          mx = warp_max(mx);
+        } else {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
         if (lane == 0) rmax[q4 * C::GP + hh] = mx;
       }
       named_bar_sync(set_bar, 128);
