@@ -99,7 +99,7 @@ typedef struct qsa_b200_decode_args {
 
 /* Bytes of device workspace qsa_b200_decode needs, each part 256-byte
  * aligned: the tensor-core kernel's row map (one int32 token slot per Top-K
- * entry: rows x chunks x 512 entries, 256 for group 16) and its tile flags
+ * entry: rows x chunks x 512 entries) and its tile flags
  * (16 bytes per row and chunk), then, when a Top-K row spans more than one
  * chunk, the split partial outputs and log-sum-exps.
  * 0 only for the CUDA-core kernel without a split. Negative on invalid

@@ -71,7 +71,7 @@ constexpr int kTileBytes = kTile * kHeadDim;  // 16 KiB of FP8
 constexpr int kTermsQ = 2;                    // FP8 terms per query value (exact for bf16)
 constexpr int kTermsP = 4;                    // FP8 terms per probability
 constexpr int kMeta = 4;                      // metadata ring depth (items)
-constexpr int kTmemBufs = 3;                  // TMEM accumulator buffers (items)
+constexpr int kMaxTmemBufs = 3;               // TMEM accumulator buffers (items), at most
 constexpr int kDecoderWarp = 0;
 constexpr int kLoaders = 6;                   // loader warps 1 .. kLoaders
 constexpr int kMmaWarp = 1 + kLoaders;
@@ -107,12 +107,16 @@ struct Cfg {
   static_assert(kThreads % 128 == 0, "whole warpgroups, so the four sub-partitions hold equal shares");
   static constexpr int NS = ((G * kTermsQ + 15) / 16) * 16;  // N of the S MMA (rows of Qs)
   static constexpr int NO = ((G * kTermsP + 15) / 16) * 16;  // N of the O MMA (rows of a Ps tile)
-  static constexpr int kTiles = G <= 8 ? 4 : 2;             // tiles per item
+  static constexpr int kTiles = 4;                          // tiles per item
   static constexpr int kChunk = kTiles * kTile;             // Top-K entries per item
   static constexpr int kBufCols = (kTiles * NS + NO + 31) / 32 * 32;  // S tiles + O, per TMEM buffer
+  // three accumulator buffers where they fit the 512 TMEM columns, else two
+  // (groups above 8: 128 score + up to 64 output columns per item)
+  static constexpr int kTmemBufs = 3 * kBufCols <= 512 ? 3 : 2;
   static constexpr int kTmemCols = pow2_at_least(kTmemBufs * kBufCols);
   static constexpr int kQsBytes = NS * 128;
-  static_assert(kTiles * NS == 64 && NO % 16 == 0 && NO <= 64, "TMEM budget and MMA N");
+  static_assert(kTiles * NS <= 128 && NO % 16 == 0 && NO <= 64, "TMEM budget and MMA N");
+  static_assert(kSoftmaxSets == 2 || kTiles * NS == 64, "a single softmax set loads its scores at once");
   static_assert(GP * kTermsQ <= NS && GP * kTermsP <= NO, "a padding head fits the S and O columns");
   static constexpr int kHalfHeads = GP / kSoftmaxSets;   // heads of one softmax set
   static constexpr int kHeadCols = kHalfHeads * kTermsP;  // O columns of one softmax warp's heads
@@ -123,8 +127,8 @@ struct Cfg {
   // score columns of one set's heads in one tile, and the stride between
   // tiles in the warp's score registers
   static constexpr int kSetCols = kHalfHeads * kTermsQ;
-  static constexpr int kRawStride = kSoftmaxSets == 1 ? NS : 32 / kTiles;  // 4 x 8 or 2 x 16 columns
-  static_assert(kSoftmaxSets == 1 || kSetCols <= kRawStride, "two-set score loads: 4 x 8 or 2 x 16 columns");
+  static constexpr int kRawStride = kSoftmaxSets == 1 ? NS : kSetCols <= 8 ? 8 : 16;  // 4 x 8 or 4 x 16 columns
+  static_assert(kSoftmaxSets == 1 || kSetCols <= kRawStride, "two-set score loads: 4 x 8 or 4 x 16 columns");
   static constexpr int kPsBytes = kTiles * NO * 128;
   // shared memory layout (offsets from a 1024-byte aligned base); every
   // region starts on a 128-byte boundary, the MMA operands on 1024
@@ -137,7 +141,7 @@ struct Cfg {
   static constexpr int kRedSum = align128(kRedMax + 2 * kSoftmaxWarps * GP * 4);  // float [2][kSoftmaxWarps][GP]
   static constexpr int kBars = align128(kRedSum + 2 * kSoftmaxWarps * GP * 4);
   static constexpr int kMaxSlots = 16;
-  static constexpr int kNumBars = 2 * kMaxSlots + 2 * kMeta + 3 * kTmemBufs + 2;
+  static constexpr int kNumBars = 2 * kMaxSlots + 2 * kMeta + 3 * kMaxTmemBufs + 2;
   // tmem address (+0), abort flag (+8), item ids of the metadata slots
   // (+16, kMeta ints)
   static constexpr int kMisc = kBars + kNumBars * 8;
@@ -295,9 +299,9 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
   uint64_t* meta_full = bars + 2 * C::kMaxSlots;   // [kMeta] decoder -> loaders, MMA, softmax
   uint64_t* meta_empty = meta_full + kMeta;        // [kMeta] loaders + MMA commit + softmax -> decoder
   uint64_t* s_full = meta_empty + kMeta;           // [kTmemBufs] MMA commit -> softmax
-  uint64_t* o_full = s_full + kTmemBufs;           // [kTmemBufs] MMA commit -> epilogue
-  uint64_t* tmem_empty = o_full + kTmemBufs;       // [kTmemBufs] epilogue (128 arrivals) -> MMA
-  uint64_t* p_full = tmem_empty + kTmemBufs;       // [2] softmax -> MMA (Ps double buffer)
+  uint64_t* o_full = s_full + kMaxTmemBufs;        // [kTmemBufs] MMA commit -> epilogue
+  uint64_t* tmem_empty = o_full + kMaxTmemBufs;    // [kTmemBufs] epilogue (softmax threads) -> MMA
+  uint64_t* p_full = tmem_empty + kMaxTmemBufs;    // [2] softmax -> MMA (Ps double buffer)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMisc + 8);
   volatile int* item_ids = reinterpret_cast<volatile int*>(smem + C::kMisc + 16);  // [kMeta]
@@ -328,7 +332,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       mbar_init(meta_full + m, 1);
       mbar_init(meta_empty + m, kLoaders + 1 + C::kSoftmaxSets);
     }
-    for (int b = 0; b < kTmemBufs; ++b) {
+    for (int b = 0; b < C::kTmemBufs; ++b) {
       mbar_init(s_full + b, 1);
       mbar_init(o_full + b, 1);
       mbar_init(tmem_empty + b, 32 * C::kSoftmaxWarps);
@@ -535,8 +539,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         const uint32_t mask = item >= 0 ? tile_mask(m) : 0u;
         if (item >= 0) {
           // S(k) = K tiles of item k . Qs^T
-          const int tb = k % kTmemBufs;
-          const int ut = k / kTmemBufs;
+          const int tb = k % C::kTmemBufs;
+          const int ut = k / C::kTmemBufs;
           if (ut > 0 && !wait_or_abort(tmem_empty + tb, (uint32_t)((ut - 1) & 1), abort_flag)) {
             failed = true;
             break;
@@ -570,7 +574,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
           // O^T(k-1) += V tiles of item k-1 ^T . Ps^T
           const int jt = k - 1;
           const int pb = jt & 1;
-          const int tb = jt % kTmemBufs;
+          const int tb = jt % C::kTmemBufs;
           if (!wait_or_abort(p_full + pb, (uint32_t)((jt >> 1) & 1), abort_flag)) {
             failed = true;
             break;
@@ -632,9 +636,9 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     float e_m[C::kHalfHeads], e_l[C::kHalfHeads];
     __nv_bfloat16 e_gate[C::kHalfHeads];
     auto epilogue = [&]() {
-      const int tb = e_k % kTmemBufs;
+      const int tb = e_k % C::kTmemBufs;
       if (!failed)
-        failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + tb, (uint32_t)((e_k / kTmemBufs) & 1), abort_flag));
+        failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + tb, (uint32_t)((e_k / C::kTmemBufs) & 1), abort_flag));
       if (failed) return;
       tc_fence_after();
       // the O columns of this warp's heads (their kTermsP terms each)
@@ -666,7 +670,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       }
     };
     for (int k = 0; k < n_my; ++k) {
-      const int tb = k % kTmemBufs;
+      const int tb = k % C::kTmemBufs;
       const int pb = k & 1;
       const int m = k % kMeta;
       const Item w = item_of(p, item_at(k));
@@ -683,7 +687,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       // named barriers must still match) but skips tensor memory.
       if (!failed) {
         const bool ok = wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag) &&
-                        wait_or_abort(s_full + tb, (uint32_t)((k / kTmemBufs) & 1), abort_flag);
+                        wait_or_abort(s_full + tb, (uint32_t)((k / C::kTmemBufs) & 1), abort_flag);
         failed = !__all_sync(0xffffffffu, ok);
       }
       tc_fence_after();
@@ -693,24 +697,35 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
 #pragma unroll
       for (int hh = 0; hh < kSH; ++hh) qi[hh] = h0 + hh < G ? qinv[m * G + h0 + hh] : 0.f;
       // this set's score columns of every tile: (tile j, head hh, term t) at
-      // raw[j * kRawStride + hh * kTermsQ + t]
-      float raw[C::kTiles * C::kRawStride];
-      if (!failed) {
-        const uint32_t s0 = tmem + lane_base + tb * C::kBufCols + h0 * kTermsQ;
-        if constexpr (C::kSoftmaxSets == 1)
-          tmem_ld_wait<C::kTiles * C::NS>(s0, raw);
-        else if constexpr (C::kTiles == 4)
-          tmem_ld_4x8_wait(s0, C::NS, raw);
-        else
-          tmem_ld_2x16_wait(s0, C::NS, raw);
-      }
+      // raw[j * kRawStride + hh * kTermsQ + t] -- all tiles in one load, or
+      // (16 columns a tile, groups above 8) one tile at a time for registers
+      const uint32_t s0 = tmem + lane_base + tb * C::kBufCols + h0 * kTermsQ;
       float sc[C::kTiles][kSH];
+      if constexpr (C::kSoftmaxSets == 2 && C::kRawStride == 16) {
 #pragma unroll
-      for (int j = 0; j < C::kTiles; ++j) {
-        const bool ok = !failed && ((mask >> j) & 1u) && rowtab[m * C::kChunk + j * kTile + tk] >= 0;
+        for (int j = 0; j < C::kTiles; ++j) {
+          float raw[16];
+          if (!failed) tmem_ld_wait<16>(s0 + j * C::NS, raw);
+          const bool ok = !failed && ((mask >> j) & 1u) && rowtab[m * C::kChunk + j * kTile + tk] >= 0;
 #pragma unroll
-        for (int hh = 0; hh < kSH; ++hh)
-          sc[j][hh] = ok ? combine_q(&raw[j * C::kRawStride + hh * kTermsQ]) * qi[hh] : -INFINITY;
+          for (int hh = 0; hh < kSH; ++hh)
+            sc[j][hh] = ok ? combine_q(&raw[hh * kTermsQ]) * qi[hh] : -INFINITY;
+        }
+      } else {
+        float raw[C::kTiles * C::kRawStride];
+        if (!failed) {
+          if constexpr (C::kSoftmaxSets == 1)
+            tmem_ld_wait<C::kTiles * C::NS>(s0, raw);
+          else
+            tmem_ld_4x8_wait(s0, C::NS, raw);
+        }
+#pragma unroll
+        for (int j = 0; j < C::kTiles; ++j) {
+          const bool ok = !failed && ((mask >> j) & 1u) && rowtab[m * C::kChunk + j * kTile + tk] >= 0;
+#pragma unroll
+          for (int hh = 0; hh < kSH; ++hh)
+            sc[j][hh] = ok ? combine_q(&raw[j * C::kRawStride + hh * kTermsQ]) * qi[hh] : -INFINITY;
+        }
       }
       // exact max per head over the chunk (one partial maximum per warp of the set)
       float* rmax = red_max + (pb * C::kSoftmaxWarps + half * 4) * C::GP + h0;
@@ -965,7 +980,7 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
 
 }  // namespace
 
-int tc_chunk_tokens(int group) { return group <= 8 ? 4 * kTile : 2 * kTile; }
+int tc_chunk_tokens(int) { return 4 * kTile; }
 
 bool tc_supports_group(int group) {
   return (group >= 1 && group <= 8) || (group <= 16 && group % 2 == 0);

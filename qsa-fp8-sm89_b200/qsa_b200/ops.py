@@ -156,9 +156,8 @@ def tc_supports_group(group: int) -> bool:
 
 
 def chunk_tokens(num_q_heads, num_kv_heads) -> int:
-    """Top-K entries one work item covers: 512 for GQA groups up to 8, 256
-    for larger groups (their score tiles fill more tensor memory)."""
-    return 512 if num_q_heads // num_kv_heads <= 8 else 256
+    """Top-K entries one work item covers: 512 for every group size."""
+    return 512
 
 
 def workspace_bytes(rows, num_q_heads, num_kv_heads, topk, kernel="auto") -> int:

@@ -129,16 +129,14 @@ def test_workspace_sizes():
     n = 4 * 32 * 3
     rowmap = 4 * 3 * 512 * 4 + 256
     assert capi.workspace_bytes(a) == rowmap + n * 512 + n * 4 == ops.workspace_bytes(4, 32, 8, 1100)
-    a.num_q_heads = 128  # group 16: 256-entry chunks
-    n = 4 * 128 * 5
-    rowmap = 4 * 5 * 256 * 4 + 512
-    assert capi.workspace_bytes(a) == rowmap + n * 512 + n * 4 == ops.workspace_bytes(4, 128, 8, 1100)
-    a.num_q_heads = 96  # group 12: tensor-core kernel, 256-entry chunks
-    n = 4 * 96 * 5
-    assert capi.workspace_bytes(a) == rowmap + n * 512 + n * 4 == ops.workspace_bytes(4, 96, 8, 1100)
-    a.num_q_heads = 72  # group 9: CUDA-core kernel (256-entry chunks), no row map
-    n = 4 * 72 * 5
-    assert capi.workspace_bytes(a) == n * 512 + -(-n * 4 // 256) * 256 == ops.workspace_bytes(4, 72, 8, 1100)
+    a256 = lambda x: -(-x // 256) * 256
+    for hq in (128, 96):  # groups 16 and 12: tensor-core kernel, 512-entry chunks like every group
+        a.num_q_heads = hq
+        n = 4 * hq * 3
+        assert capi.workspace_bytes(a) == rowmap + n * 512 + a256(n * 4) == ops.workspace_bytes(4, hq, 8, 1100)
+    a.num_q_heads = 72  # group 9: CUDA-core kernel, no row map
+    n = 4 * 72 * 3
+    assert capi.workspace_bytes(a) == n * 512 + a256(n * 4) == ops.workspace_bytes(4, 72, 8, 1100)
 
 
 def test_torch_ops_register_and_refuse_cpu_tensors():
