@@ -3,11 +3,13 @@
 //
 // The index decode runs first, in its own small kernel (qsa_rowmap_kernel):
 // every Top-K entry becomes its physical token slot phys * P + t % P (or -1)
-// in a row map in the workspace, in parallel over the whole GPU. The decode
-// kernel is a programmatic dependent launch of it: its prologue (barriers,
-// TMEM, tensor maps) overlaps the row map, and only the decoder warp waits
-// for the row map (griddepcontrol.wait) before its first read of it. The
-// pipeline then needs no dependent global reads of its own.
+// in a row map in the workspace, in parallel over the whole GPU, before the
+// K/V gathers saturate HBM (under that load a dependent global read waits
+// several microseconds). The decode kernel is a programmatic dependent launch
+// of it: its prologue (barriers, TMEM, tensor maps) overlaps the row map, and
+// only the decoder warp waits for the row map (griddepcontrol.wait) before
+// its first read of it. The pipeline then needs no dependent global reads of
+// its own.
 //
 // Work item = (Top-K row, KV head, chunk of up to kTiles*128 Top-K entries).
 // Each CTA (one per SM) takes items blockIdx.x, blockIdx.x + gridDim.x, ...
@@ -34,14 +36,15 @@
 //   MMA warp           one thread issues S = K_tile . Qs^T into TMEM for every
 //                      K tile of item k, then O^T += V_tile^T . Ps^T for item
 //                      k-1 (its probabilities are ready by then);
-//   softmax warps      one per TMEM lane quadrant (a second set, if
-//                      configured, splits the score tiles and epilogue heads
-//                      with the first): softmax over the chunk's scores (exact
-//                      max and sum), probabilities as FP8 terms of p*256
-//                      (operand Ps); then the epilogue of the previous item
-//                      (its O is complete by then): recombine, normalise,
-//                      v_scale, sigmoid gate, bf16 store (or a partial for the
-//                      split combine).
+//   softmax warps      one set of four (one per TMEM lane quadrant), or for
+//                      G >= 5 two independent sets, each taking half of the
+//                      heads (odd G padded by one head) with its own named
+//                      barrier: softmax over the chunk's scores (exact max and
+//                      sum), probabilities as FP8 terms of p*256 (operand Ps);
+//                      then the epilogue of the previous item (its O is
+//                      complete by then): recombine, normalise, v_scale,
+//                      sigmoid gate, bf16 store (or a partial for the split
+//                      combine).
 //
 // Every selected 128-byte K/V row is read from HBM once and shared by the G
 // query heads. Q and P keep their precision through a split into E4M3 terms:
@@ -52,7 +55,8 @@
 //
 // Synchronisation is by mbarriers: kv_full/kv_empty per K/V ring slot,
 // meta_full/meta_empty per metadata slot, s_full/o_full/tmem_empty per TMEM
-// accumulator buffer (three), p_full per probability buffer (two). Every wait
+// accumulator buffer (three, or two for G > 8), p_full per probability buffer
+// (two). Every wait
 // is bounded; a CTA that gives up records an error in the device error word,
 // raises a CTA-wide abort flag so the other roles leave their loops, waits for
 // its own copies in flight, frees its TMEM and returns.
