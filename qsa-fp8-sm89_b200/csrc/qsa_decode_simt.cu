@@ -161,8 +161,10 @@ __global__ void __launch_bounds__(32 * kCombineWarps) qsa_combine_kernel(DecodeP
 #pragma unroll 4
     for (int c = 0; c < p.num_chunks; ++c) {
       const float l = __ldg(lse + c);
+      // an empty chunk (log-sum -inf) may have no partial output written
+      if (l == -INFINITY) continue;
       const float4 v = __ldg(po + c * (kHeadDim / 4));
-      const float w = l == -INFINITY ? 0.f : exp2f(l - mx);
+      const float w = exp2f(l - mx);
       wsum += w;
       acc.x = fmaf(w, v.x, acc.x);
       acc.y = fmaf(w, v.y, acc.y);

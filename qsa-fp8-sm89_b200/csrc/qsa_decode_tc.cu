@@ -7,13 +7,15 @@
 // K/V gathers saturate HBM (under that load a dependent global read waits
 // several microseconds). The decode kernel is a programmatic dependent launch
 // of it: its prologue (barriers, TMEM, tensor maps) overlaps the row map, and
-// only the decoder warp waits for the row map (griddepcontrol.wait) before
-// its first read of it. The pipeline then needs no dependent global reads of
+// only the decoder warp (and, for split rows, the softmax warps, which read
+// the tile flags) waits for the row map (griddepcontrol.wait) before its
+// first read of it. The pipeline then needs no dependent global reads of
 // its own.
 //
 // Work item = (Top-K row, KV head, chunk of up to kTiles*128 Top-K entries).
 // Each CTA (one per SM) takes items blockIdx.x, blockIdx.x + gridDim.x, ...
-// (its k-th item is blockIdx.x + k * gridDim.x, k < n_my); the item id
+// (its i-th item is blockIdx.x + i * gridDim.x, i < n_my), except, for split
+// rows, the chunks that hold no valid entry (see ItemWalk); the item id
 // travels with the item's metadata slot, and an id of -1 after the last item
 // ends the loaders' and the MMA warp's loops. Four roles overlap across items:
 //
@@ -179,6 +181,59 @@ __device__ __forceinline__ Item item_of(const DecodeParams& p, int item) {
   return it;
 }
 
+// The walk over one CTA's items when rows are split (num_chunks > 1): local
+// index i is item blockIdx.x + i * gridDim.x (i < n_my), and an item whose
+// chunk holds no valid tile (a chunk past a ragged row's end) is left out.
+// The decoder never publishes such an item and every role that counts items
+// walks the same sequence, so their ring positions agree. The tile flags of
+// the next 32 local items are loaded a window ahead; the walk waits on memory
+// only for its first window. Unsplit rows walk every item (an empty row still
+// writes its zeros), by plain counting.
+struct ItemWalk {
+  int base;        // first local index of the current window
+  uint32_t live;   // bit b: local item base + b is still to be returned
+  uint32_t ahead;  // this lane's tile-flags word of local item base + 32 + lane
+};
+
+__device__ __forceinline__ uint32_t chunk_flags(const DecodeParams& p, int item) {
+  const Item w = item_of(p, item);
+  return *reinterpret_cast<const uint32_t*>(p.tile_flags + ((int64_t)w.row * p.num_chunks + w.chunk) * 16);
+}
+
+// Must follow griddepcontrol.wait (the flags come from the row-map kernel).
+__device__ __forceinline__ void walk_init(ItemWalk& wk, const DecodeParams& p, int n_my, int lane) {
+  wk.base = -32;
+  wk.live = 0;
+  wk.ahead = lane < n_my ? chunk_flags(p, (int)blockIdx.x + lane * (int)gridDim.x) : 0u;
+}
+
+// Next local index of the walk, -1 at its end. The decoder (mark_skipped)
+// also gives each left-out item's partials a log-sum of -inf, which tells the
+// split combine that the chunk is empty.
+template <int G>
+__device__ __forceinline__ int walk_next(ItemWalk& wk, const DecodeParams& p, int n_my, int lane,
+                                         bool mark_skipped) {
+  while (wk.live == 0u) {
+    wk.base += 32;
+    if (wk.base >= n_my) return -1;
+    const int li = wk.base + lane;
+    const bool in = li < n_my;
+    const bool keep = in && wk.ahead != 0u;
+    wk.live = __ballot_sync(0xffffffffu, keep);
+    if (mark_skipped && in && !keep) {
+      const Item w = item_of(p, (int)blockIdx.x + li * (int)gridDim.x);
+#pragma unroll 1
+      for (int h = 0; h < G; ++h)
+        p.part_lse[((int64_t)w.row * p.num_q_heads + w.g * G + h) * p.num_chunks + w.chunk] = -INFINITY;
+    }
+    const int la = li + 32;
+    wk.ahead = la < n_my ? chunk_flags(p, (int)blockIdx.x + la * (int)gridDim.x) : 0u;
+  }
+  const int b = __ffs(wk.live) - 1;
+  wk.live &= wk.live - 1u;
+  return wk.base + b;
+}
+
 // ------------------------------------------------------------------ PTX ----
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
@@ -283,7 +338,9 @@ __device__ __forceinline__ float combine_p(const float* v) {
   return v[0] + v[1] * 0.0625f + v[2] * 0.00390625f + v[3] * 0.00048828125f;
 }
 
-template <int G>
+// kSplit: rows are split into several chunks (num_chunks > 1). A separate
+// instance keeps the unsplit loop free of the walk's code.
+template <int G, bool kSplit>
 __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     qsa_decode_tc_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
                          const __grid_constant__ CUtensorMap tmap_v, int num_items) {
@@ -357,6 +414,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
+  constexpr bool split = kSplit;  // items are walked (ItemWalk), else counted
 
   if (warp == kDecoderWarp) {
     // =============================== decoder ================================
@@ -370,19 +428,29 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       }
     };
     uint2 q_n[G];
-    load_q(item_at(0), q_n);
-    // the row map is written by the preceding kernel of this programmatic
-    // dependent launch
+    load_q(item_at(0), q_n);  // the walk's first item unless it is left out
+    // the row map and the tile flags are written by the preceding kernel of
+    // this programmatic dependent launch
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
-    int k = 0;
+    ItemWalk wk;
+    int nx = 0;  // local index of the next published item
+    if (split) {
+      walk_init(wk, p, n_my, lane);
+      nx = walk_next<G>(wk, p, n_my, lane, true);
+      if (nx > 0) load_q(item_at(nx), q_n);
+    }
+    int k = 0;  // published items so far
     for (;; ++k) {
-      const bool last = k == n_my;
-      const int item = item_at(k);
+      const bool last = nx < 0;
+      const int item = last ? 0 : item_at(nx);
       const int m = k % kMeta;
       uint2 q_c[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) q_c[h] = q_n[h];
-      if (!last) load_q(item_at(k + 1), q_n);
+      if (!last) {
+        nx = split ? walk_next<G>(wk, p, n_my, lane, true) : (nx + 1 < n_my ? nx + 1 : -1);
+        if (nx >= 0) load_q(item_at(nx), q_n);
+      }
 
       // query heads -> FP8 terms (lane owns dims 4*lane .. 4*lane+3)
       uint32_t qpk[G][kTermsQ];
@@ -673,11 +741,18 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         }
       }
     };
-    for (int k = 0; k < n_my; ++k) {
+    ItemWalk wk;
+    if (split) {
+      asm volatile("griddepcontrol.wait;\n" ::: "memory");  // the walk reads tile flags
+      walk_init(wk, p, n_my, lane);
+    }
+    for (int k = 0;; ++k) {
+      const int li = split ? walk_next<G>(wk, p, n_my, lane, false) : (k < n_my ? k : -1);
+      if (li < 0) break;
       const int tb = k % C::kTmemBufs;
       const int pb = k & 1;
       const int m = k % kMeta;
-      const Item w = item_of(p, item_at(k));
+      const Item w = item_of(p, item_at(li));
       // the gate of this warp's heads, needed by the epilogue one iteration later
       __nv_bfloat16 gate[C::kHalfHeads];
       if (p.num_chunks == 1) {
@@ -949,7 +1024,11 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(qsa_decode_tc_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemAlloc);
+    e = cudaFuncSetAttribute(qsa_decode_tc_kernel<G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmemAlloc);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(qsa_decode_tc_kernel<G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmemAlloc);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
@@ -979,7 +1058,8 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qsa_decode_tc_kernel<G>, p, mk, mv, (int)items);
+  return p.num_chunks > 1 ? cudaLaunchKernelEx(&cfg, qsa_decode_tc_kernel<G, true>, p, mk, mv, (int)items)
+                          : cudaLaunchKernelEx(&cfg, qsa_decode_tc_kernel<G, false>, p, mk, mv, (int)items);
 }
 
 }  // namespace

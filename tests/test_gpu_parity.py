@@ -343,6 +343,30 @@ def test_duplicates_and_masked_entries_count_per_occurrence():
         check_close(bits(out), ref, what=f"dups/{kernel}")
 
 
+@pytest.mark.parametrize("hq,kernel", [(32, "tc"), (64, "tc"), (32, "simt")])
+def test_split_rows_with_empty_chunks(hq, kernel):
+    """Rows split into 512-entry chunks where whole chunks hold no valid
+    entry: a masked middle chunk, only the last chunk valid, a fully masked
+    row and a row whose request id is invalid. The empty chunks drop out of
+    the split combine; an empty row still comes back as zeros."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=21 + hq, rows=5, hq=hq, hkv=8, ppr=120, topk=1600, mode="sample")
+    idx = w.indices.clone()
+    idx[0, 512:1024] = -1
+    idx[1, :1536] = -1
+    idx[2, :] = -1
+    t2r = w.t2r.clone()
+    t2r[4] = -1
+    out = qsa_decode(w.q, w.k, w.v, 1.0, 1.0, w.btable, t2r, idx, w.gate, kernel=kernel)
+    torch.cuda.synchronize()
+    ref = O.attention(bits(w.q), u8(w.k).reshape(w.k.shape), u8(w.v).reshape(w.v.shape), 1.0, 1.0,
+                      w.btable.cpu().numpy(), t2r.cpu().numpy(), idx.cpu().numpy(), bits(w.gate))
+    check_close(bits(out), ref, what=f"empty chunks/G={hq // 8}/{kernel}")
+    assert np.all(bits(out)[[2, 4]] == 0)
+
+
 def test_cuda_graph_replay_matches_eager():
     from qsa_b200 import qsa_decode
     from qsa_b200.inputs import make_workload
