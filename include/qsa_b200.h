@@ -99,9 +99,9 @@ typedef struct qsa_b200_decode_args {
 
 /* Bytes of device workspace qsa_b200_decode needs, each part 256-byte
  * aligned: the tensor-core kernel's row map (one int32 token slot per Top-K
- * entry: rows x chunks x 512 entries) and its tile flags
- * (16 bytes per row and chunk), then, when a Top-K row spans more than one
- * chunk, the split partial outputs and log-sum-exps.
+ * entry: rows x chunks x 512 entries), its tile flags (16 bytes per row and
+ * chunk) and its item claim counter (256 bytes), then, when a Top-K row spans
+ * more than one chunk, the split partial outputs and log-sum-exps.
  * 0 only for the CUDA-core kernel without a split. Negative on invalid
  * arguments. */
 QSA_B200_API int64_t qsa_b200_workspace_bytes(const qsa_b200_decode_args* args);

@@ -133,6 +133,7 @@ void fill_params(const qsa_b200_decode_args* a, DecodeParams* p) {
   p->rowmap = nullptr;
   p->rowmap_stride = p->num_chunks * p->chunk_tokens;
   p->tile_flags = nullptr;
+  p->item_counter = nullptr;
   p->err = nullptr;
 }
 
@@ -142,7 +143,7 @@ bool uses_tc(const qsa_b200_decode_args* a, int group) {
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-// Workspace parts: [row map, tile flags][partial outputs][partial log-sum-exps].
+// Workspace parts: [row map, tile flags, claim counter][partial outputs][partial log-sum-exps].
 struct WorkspaceLayout {
   int64_t rowmap_bytes, part_o_bytes, part_lse_bytes;
   int64_t total() const { return rowmap_bytes + part_o_bytes + part_lse_bytes; }
@@ -150,7 +151,8 @@ struct WorkspaceLayout {
 
 WorkspaceLayout workspace_for(const DecodeParams& p, bool tc) {
   WorkspaceLayout w{0, 0, 0};
-  if (tc) w.rowmap_bytes = align256((int64_t)p.rows * p.rowmap_stride * 4) + align256((int64_t)p.rows * p.num_chunks * 16);
+  if (tc)
+    w.rowmap_bytes = align256((int64_t)p.rows * p.rowmap_stride * 4) + align256((int64_t)p.rows * p.num_chunks * 16) + 256;
   if (p.num_chunks > 1) {
     const int64_t n = (int64_t)p.rows * p.num_q_heads * p.num_chunks;
     w.part_o_bytes = align256(n * 128 * 4);
@@ -214,6 +216,8 @@ int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t wo
     if (use_tc) {
       p.rowmap = reinterpret_cast<int32_t*>(ws);
       p.tile_flags = reinterpret_cast<uint8_t*>(ws + align256((int64_t)p.rows * p.rowmap_stride * 4));
+      p.item_counter = reinterpret_cast<int*>(reinterpret_cast<char*>(p.tile_flags) +
+                                              align256((int64_t)p.rows * p.num_chunks * 16));
     }
     if (p.num_chunks > 1) {
       p.part_o = reinterpret_cast<float*>(ws + lay.rowmap_bytes);

@@ -13,11 +13,14 @@
 // its own.
 //
 // Work item = (Top-K row, KV head, chunk of up to kTiles*128 Top-K entries).
-// Each CTA (one per SM) takes items blockIdx.x, blockIdx.x + gridDim.x, ...
-// (its i-th item is blockIdx.x + i * gridDim.x, i < n_my), except, for split
-// rows, the chunks that hold no valid entry (see ItemWalk); the item id
-// travels with the item's metadata slot, and an id of -1 after the last item
-// ends the loaders' and the MMA warp's loops. Four roles overlap across items:
+// With unsplit rows each CTA (one per SM) takes items blockIdx.x,
+// blockIdx.x + gridDim.x, ... (its k-th item is blockIdx.x + k * gridDim.x,
+// k < n_my). With split rows it walks windows of items claimed from a
+// per-call counter and leaves out the chunks that hold no valid entry (see
+// ItemWalk). The decoder publishes the item id with the item's metadata
+// slot, and an id of -1 after the last item ends the loaders', the MMA
+// warp's and (split rows) the softmax warps' loops. Four roles overlap
+// across items:
 //
 //   decoder (warp 0)   for a kMeta-deep metadata ring: TMA bulk copies bring
 //                      the item's chunk of the row map into the slot's row
@@ -181,57 +184,86 @@ __device__ __forceinline__ Item item_of(const DecodeParams& p, int item) {
   return it;
 }
 
-// The walk over one CTA's items when rows are split (num_chunks > 1): local
-// index i is item blockIdx.x + i * gridDim.x (i < n_my), and an item whose
-// chunk holds no valid tile (a chunk past a ragged row's end) is left out.
-// The decoder never publishes such an item and every role that counts items
-// walks the same sequence, so their ring positions agree. The tile flags of
-// the next 32 local items are loaded a window ahead; the walk waits on memory
-// only for its first window. Unsplit rows walk every item (an empty row still
-// writes its zeros), by plain counting.
+// The decoder's walk over the items when rows are split (num_chunks > 1).
+// Items are taken in windows of kWalkWindow claim indices. Claim index c
+// stands for (row, chunk) rc = c % (rows * num_chunks) and KV head
+// c / (rows * num_chunks), so a window holds consecutive chunks of one row
+// for one head. A CTA's first window is static (c from blockIdx.x *
+// kWalkWindow); later ones are claimed from the per-call counter, from
+// gridDim.x * kWalkWindow on, so a CTA that draws long rows (or runs slow)
+// takes fewer: ragged rows make the work per window uneven. An item whose
+// chunk holds no valid tile (past a ragged row's end) is left out, never
+// published, and its partials get a log-sum of -inf, which tells the split
+// combine that the chunk is empty. Each window's claim is issued two windows
+// and its tile flags one window before it is walked, so neither wait shows.
+constexpr int kWalkWindow = 4;
 struct ItemWalk {
-  int base;        // first local index of the current window
-  uint32_t live;   // bit b: local item base + b is still to be returned
-  uint32_t ahead;  // this lane's tile-flags word of local item base + 32 + lane
+  int base;             // first claim index of the current window
+  uint32_t live;        // bit b: claim index base + b is still to be published
+  int next_base;        // first claim index of the next window
+  uint32_t next_flags;  // lane b < kWalkWindow: tile flags word of claim index next_base + b
+  int claim;            // lane 0: first claim index of the window after next (in flight)
 };
 
-__device__ __forceinline__ uint32_t chunk_flags(const DecodeParams& p, int item) {
-  const Item w = item_of(p, item);
-  return *reinterpret_cast<const uint32_t*>(p.tile_flags + ((int64_t)w.row * p.num_chunks + w.chunk) * 16);
+__device__ __forceinline__ int claim_rc(const DecodeParams& p, int c) { return c % (p.rows * p.num_chunks); }
+__device__ __forceinline__ int claim_item(const DecodeParams& p, int c) {
+  return claim_rc(p, c) * p.num_kv_heads + c / (p.rows * p.num_chunks);
+}
+__device__ __forceinline__ uint32_t claim_flags(const DecodeParams& p, int c, int num_items, int lane) {
+  return (lane < kWalkWindow && c < num_items)
+             ? *reinterpret_cast<const uint32_t*>(p.tile_flags + (int64_t)claim_rc(p, c) * 16)
+             : 0u;
+}
+__device__ __forceinline__ int claim_window(const DecodeParams& p) {
+  return (int)gridDim.x * kWalkWindow + atomicAdd(p.item_counter, kWalkWindow);
 }
 
-// Must follow griddepcontrol.wait (the flags come from the row-map kernel).
-__device__ __forceinline__ void walk_init(ItemWalk& wk, const DecodeParams& p, int n_my, int lane) {
-  wk.base = -32;
+// Must follow griddepcontrol.wait (the flags and the counter come from the
+// row-map kernel).
+__device__ __forceinline__ void walk_init(ItemWalk& wk, const DecodeParams& p, int num_items, int lane) {
+  wk.base = 0;
   wk.live = 0;
-  wk.ahead = lane < n_my ? chunk_flags(p, (int)blockIdx.x + lane * (int)gridDim.x) : 0u;
+  wk.next_base = (int)blockIdx.x * kWalkWindow;
+  wk.next_flags = claim_flags(p, wk.next_base + lane, num_items, lane);
+  wk.claim = lane == 0 ? claim_window(p) : 0;
 }
 
-// Next local index of the walk, -1 at its end. The decoder (mark_skipped)
-// also gives each left-out item's partials a log-sum of -inf, which tells the
-// split combine that the chunk is empty.
+// The next item of the walk, -1 at its end.
 template <int G>
-__device__ __forceinline__ int walk_next(ItemWalk& wk, const DecodeParams& p, int n_my, int lane,
-                                         bool mark_skipped) {
+__device__ __forceinline__ int walk_next(ItemWalk& wk, const DecodeParams& p, int num_items, int lane) {
   while (wk.live == 0u) {
-    wk.base += 32;
-    if (wk.base >= n_my) return -1;
-    const int li = wk.base + lane;
-    const bool in = li < n_my;
-    const bool keep = in && wk.ahead != 0u;
+    if (wk.next_base >= num_items) return -1;
+    // the next window becomes the current one
+    wk.base = wk.next_base;
+    const int c = wk.base + lane;
+    const bool in = lane < kWalkWindow && c < num_items;
+    const bool keep = in && wk.next_flags != 0u;
     wk.live = __ballot_sync(0xffffffffu, keep);
-    if (mark_skipped && in && !keep) {
-      const Item w = item_of(p, (int)blockIdx.x + li * (int)gridDim.x);
+    if (in && !keep) {
+      const Item w = item_of(p, claim_item(p, c));
 #pragma unroll 1
       for (int h = 0; h < G; ++h)
         p.part_lse[((int64_t)w.row * p.num_q_heads + w.g * G + h) * p.num_chunks + w.chunk] = -INFINITY;
     }
-    const int la = li + 32;
-    wk.ahead = la < n_my ? chunk_flags(p, (int)blockIdx.x + la * (int)gridDim.x) : 0u;
+    // the window after it (claimed one window ago) and a claim for the one after that
+    wk.next_base = __shfl_sync(0xffffffffu, wk.claim, 0);
+    wk.next_flags = claim_flags(p, wk.next_base + lane, num_items, lane);
+    if (lane == 0 && wk.next_base < num_items) wk.claim = claim_window(p);
   }
   const int b = __ffs(wk.live) - 1;
   wk.live &= wk.live - 1u;
-  return wk.base + b;
+  return claim_item(p, wk.base + b);
+}
+
+// Named-barrier vote of count threads: true when pred holds in any of them.
+__device__ __forceinline__ bool bar_red_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0u;
 }
 
 // ------------------------------------------------------------------ PTX ----
@@ -367,7 +399,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMisc + 8);
   volatile int* item_ids = reinterpret_cast<volatile int*>(smem + C::kMisc + 16);  // [kMeta]
 
-  // items of this CTA: blockIdx.x + k * gridDim.x for k < n_my (grid <= items)
+  // unsplit rows: the items of this CTA are blockIdx.x + k * gridDim.x for
+  // k < n_my (grid <= items)
   const int n_my = (num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   auto item_at = [&](int k) { return (int)blockIdx.x + k * (int)gridDim.x; };
   float* qinv = reinterpret_cast<float*>(smem + C::kQinv);
@@ -414,7 +447,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
-  constexpr bool split = kSplit;  // items are walked (ItemWalk), else counted
+  constexpr bool split = kSplit;  // the decoder walks the items (ItemWalk), else they are counted
 
   if (warp == kDecoderWarp) {
     // =============================== decoder ================================
@@ -428,28 +461,30 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       }
     };
     uint2 q_n[G];
-    load_q(item_at(0), q_n);  // the walk's first item unless it is left out
-    // the row map and the tile flags are written by the preceding kernel of
-    // this programmatic dependent launch
+    load_q(item_at(0), q_n);  // the first item, unless the walk starts elsewhere
+    // the row map, the tile flags and the claim counter are written by the
+    // preceding kernel of this programmatic dependent launch
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     ItemWalk wk;
-    int nx = 0;  // local index of the next published item
+    // the next item to publish: unsplit rows, its local index; split rows,
+    // its id (-1: the end)
+    int nx = 0;
     if (split) {
-      walk_init(wk, p, n_my, lane);
-      nx = walk_next<G>(wk, p, n_my, lane, true);
-      if (nx > 0) load_q(item_at(nx), q_n);
+      walk_init(wk, p, num_items, lane);
+      nx = walk_next<G>(wk, p, num_items, lane);
+      if (nx >= 0 && nx != item_at(0)) load_q(nx, q_n);
     }
     int k = 0;  // published items so far
     for (;; ++k) {
       const bool last = nx < 0;
-      const int item = last ? 0 : item_at(nx);
+      const int item = last ? 0 : (split ? nx : item_at(nx));
       const int m = k % kMeta;
       uint2 q_c[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) q_c[h] = q_n[h];
       if (!last) {
-        nx = split ? walk_next<G>(wk, p, n_my, lane, true) : (nx + 1 < n_my ? nx + 1 : -1);
-        if (nx >= 0) load_q(item_at(nx), q_n);
+        nx = split ? walk_next<G>(wk, p, num_items, lane) : (nx + 1 < n_my ? nx + 1 : -1);
+        if (nx >= 0) load_q(split ? nx : item_at(nx), q_n);
       }
 
       // query heads -> FP8 terms (lane owns dims 4*lane .. 4*lane+3)
@@ -702,6 +737,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const int h0 = half * C::kHalfHeads;    // first head of this warp's set
     const int set_bar = 1 + half;           // named barrier of the set
+    const int vote_bar = 3 + half;          // named barrier of the set's votes (split rows)
     // state of the item whose epilogue is pending
     int e_k = -1, e_row = 0, e_g = 0, e_chunk = 0;
     bool e_any = false;  // the pending item has a valid tile
@@ -741,18 +777,30 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         }
       }
     };
-    ItemWalk wk;
-    if (split) {
-      asm volatile("griddepcontrol.wait;\n" ::: "memory");  // the walk reads tile flags
-      walk_init(wk, p, n_my, lane);
-    }
     for (int k = 0;; ++k) {
-      const int li = split ? walk_next<G>(wk, p, n_my, lane, false) : (k < n_my ? k : -1);
+      // unsplit rows: the local index of item k; split rows: the walk's
+      // item, which comes with the metadata slot (meta_full publishes its
+      // id). There the set's warps leave together, after the last item or
+      // once any of them failed (its id could be stale), so that their named
+      // barriers match.
+      int li;
+      if constexpr (split) {
+        const int m = k % kMeta;
+        if (!failed)
+          failed = !__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag));
+        if (bar_red_or(vote_bar, 128, failed)) {
+          failed = true;
+          break;
+        }
+        li = item_ids[m];
+      } else {
+        li = k < n_my ? k : -1;
+      }
       if (li < 0) break;
       const int tb = k % C::kTmemBufs;
       const int pb = k & 1;
       const int m = k % kMeta;
-      const Item w = item_of(p, item_at(li));
+      const Item w = item_of(p, split ? li : item_at(li));
       // the gate of this warp's heads, needed by the epilogue one iteration later
       __nv_bfloat16 gate[C::kHalfHeads];
       if (p.num_chunks == 1) {
@@ -765,7 +813,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       // scores. Once anything failed the group keeps walking its items (the
       // named barriers must still match) but skips tensor memory.
       if (!failed) {
-        const bool ok = wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag) &&
+        const bool ok = (split || wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag)) &&
                         wait_or_abort(s_full + tb, (uint32_t)((k / C::kTmemBufs) & 1), abort_flag);
         failed = !__all_sync(0xffffffffu, ok);
       }
@@ -919,6 +967,7 @@ __global__ void __launch_bounds__(kRowmapThreads) qsa_rowmap_kernel(const __grid
   // let the decode kernel launch now; it waits for this grid before reading
   // the map
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  if (blockIdx.x == 0 && threadIdx.x == 0) *p.item_counter = 0;  // the decode's claims start here
   const int quads = p.rowmap_stride / 4;
   const int64_t total = (int64_t)p.rows * quads;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -1036,7 +1085,8 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
   if (p.num_pages * p.page_size * p.num_kv_heads > 0x7fffffffll) return cudaErrorInvalidValue;
-  if (!p.rowmap || !p.tile_flags || p.rowmap_stride != p.num_chunks * C::kChunk) return cudaErrorInvalidValue;
+  if (!p.rowmap || !p.tile_flags || !p.item_counter || p.rowmap_stride != p.num_chunks * C::kChunk)
+    return cudaErrorInvalidValue;
   const int64_t rows = p.num_pages * p.page_size * p.num_kv_heads;
   CUtensorMap mk, mv;
   if (!encode_rows(&mk, p.k, rows) || !encode_rows(&mv, p.v, rows)) return cudaErrorInvalidValue;

@@ -57,6 +57,9 @@ struct DecodeParams {
   // tile of each (row, chunk), nonzero when the tile holds a valid entry;
   // 16 bytes per (row, chunk).
   uint8_t* tile_flags;
+  // Claim counter of the tensor-core kernel (workspace, zeroed by its row-map
+  // kernel): with split rows, CTAs claim windows of items from it.
+  int* item_counter;
 
   int* err;  // device error word of the current device
 };

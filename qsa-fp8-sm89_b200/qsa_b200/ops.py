@@ -163,15 +163,15 @@ def chunk_tokens(num_q_heads, num_kv_heads) -> int:
 def workspace_bytes(rows, num_q_heads, num_kv_heads, topk, kernel="auto") -> int:
     """Device workspace one call needs, each part 256-byte aligned: the row
     map of the tensor-core kernel (one int32 token slot per Top-K entry,
-    rows x chunks x chunk entries) and its tile flags (16 bytes per row and
-    chunk), then, when a Top-K row spans more than one chunk, the per-chunk
-    partial outputs and log-sum-exps."""
+    rows x chunks x chunk entries), its tile flags (16 bytes per row and
+    chunk) and its item claim counter, then, when a Top-K row spans more than
+    one chunk, the per-chunk partial outputs and log-sum-exps."""
     a256 = lambda x: -(-x // 256) * 256
     c = chunk_tokens(num_q_heads, num_kv_heads)
     chunks = 1 if topk <= c else -(-topk // c)
     group = num_q_heads // num_kv_heads
     tc = kernel == "tc" or (kernel == "auto" and tc_supports_group(group))
-    total = a256(rows * chunks * c * 4) + a256(rows * chunks * 16) if (tc and rows > 0) else 0
+    total = a256(rows * chunks * c * 4) + a256(rows * chunks * 16) + 256 if (tc and rows > 0) else 0
     if chunks > 1:
         n = rows * num_q_heads * chunks
         total += a256(n * 128 * 4) + a256(n * 4)

@@ -114,20 +114,21 @@ def test_empty_batch_is_a_no_op_without_a_device():
 
 
 def test_workspace_sizes():
-    """[row map, tile flags (tensor-core kernel)][partial outputs][partial
-    lse], each 256-byte aligned; the CUDA-core kernel needs no row map."""
+    """[row map, tile flags, claim counter (tensor-core kernel)][partial
+    outputs][partial lse], each 256-byte aligned; the CUDA-core kernel needs
+    no row map."""
     from qsa_b200 import capi, ops
 
     a = _args_cpu(topk=512, indices_stride=512)
     a.indices = a.btable = a.q = a.k_cache = a.v_cache = a.gate = a.out = ctypes.c_void_p(4096)
-    rowmap = 4 * 512 * 4 + 256
+    rowmap = 4 * 512 * 4 + 256 + 256
     assert capi.workspace_bytes(a) == rowmap == ops.workspace_bytes(4, 32, 8, 512)
     a.kernel = capi.KERNEL_SIMT
     assert capi.workspace_bytes(a) == 0 == ops.workspace_bytes(4, 32, 8, 512, kernel="simt")
     a.kernel = capi.KERNEL_AUTO
     a.topk, a.indices_stride = 1100, 1101
     n = 4 * 32 * 3
-    rowmap = 4 * 3 * 512 * 4 + 256
+    rowmap = 4 * 3 * 512 * 4 + 256 + 256
     assert capi.workspace_bytes(a) == rowmap + n * 512 + n * 4 == ops.workspace_bytes(4, 32, 8, 1100)
     a256 = lambda x: -(-x // 256) * 256
     for hq in (128, 96):  # groups 16 and 12: tensor-core kernel, 512-entry chunks like every group
