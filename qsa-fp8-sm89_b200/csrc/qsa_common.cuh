@@ -307,6 +307,18 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand without swizzle:
+// core matrices of 8 K-rows x 16 contiguous MN bytes (128 bytes); lbo_bytes
+// is the step between core matrices along K, sbo_bytes the step along MN.
+__device__ __forceinline__ uint64_t smem_desc_mn_interleave(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  return d;                // swizzle mode 0: none
+}
+
 // Instruction descriptor for kind::f8f6f4 with E4M3 A and B, FP32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int m, int n, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                             // D format: F32

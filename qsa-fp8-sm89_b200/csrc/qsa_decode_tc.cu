@@ -45,7 +45,9 @@
 //                      G >= 5 two independent sets, each taking half of the
 //                      heads (odd G padded by one head) with its own named
 //                      barrier: softmax over the chunk's scores (exact max and
-//                      sum), probabilities as FP8 terms of p*256 (operand Ps);
+//                      sum), probabilities as FP8 terms of p*256 (operand Ps:
+//                      term-major, one byte per store, for G < 8; token-major,
+//                      16 bytes per store, for G >= 8);
 //                      then the epilogue of the previous item (its O is
 //                      complete by then): recombine, normalise, v_scale,
 //                      sigmoid gate, bf16 store (or a partial for the split
@@ -115,7 +117,16 @@ struct Cfg {
   static constexpr int kThreads = 32 * (kSoftmax0 + kSoftmaxWarps);
   static_assert(kThreads % 128 == 0, "whole warpgroups, so the four sub-partitions hold equal shares");
   static constexpr int NS = ((G * kTermsQ + 15) / 16) * 16;  // N of the S MMA (rows of Qs)
-  static constexpr int NO = ((G * kTermsP + 15) / 16) * 16;  // N of the O MMA (rows of a Ps tile)
+  static constexpr int kHalfHeads = GP / kSoftmaxSets;       // heads of one softmax set
+  // Ps of the large groups is token-major (the MN-major B operand of the O
+  // MMA): each token's probability terms are contiguous, so a thread stores
+  // its set's terms of a tile in 16-byte pieces, and each set's heads are
+  // padded to whole 16-byte columns (4 heads x 4 terms). Small groups keep
+  // Ps term-major (K-major, 128-byte swizzle), one byte per store.
+  static constexpr bool kPsTokenMajor = G >= 8;
+  static constexpr int kSetN = kPsTokenMajor ? ((kHalfHeads * kTermsP + 15) / 16) * 16 : kHalfHeads * kTermsP;
+  static constexpr int NO = kPsTokenMajor ? kSoftmaxSets * kSetN
+                                          : ((G * kTermsP + 15) / 16) * 16;  // N of the O MMA (terms of a Ps tile)
   static constexpr int kTiles = 4;                          // tiles per item
   static constexpr int kChunk = kTiles * kTile;             // Top-K entries per item
   static constexpr int kBufCols = (kTiles * NS + NO + 31) / 32 * 32;  // S tiles + O, per TMEM buffer
@@ -127,7 +138,6 @@ struct Cfg {
   static_assert(kTiles * NS <= 128 && NO % 16 == 0 && NO <= 64, "TMEM budget and MMA N");
   static_assert(kSoftmaxSets == 2 || kTiles * NS == 64, "a single softmax set loads its scores at once");
   static_assert(GP * kTermsQ <= NS && GP * kTermsP <= NO, "a padding head fits the S and O columns");
-  static constexpr int kHalfHeads = GP / kSoftmaxSets;   // heads of one softmax set
   static constexpr int kHeadCols = kHalfHeads * kTermsP;  // O columns of one softmax warp's heads
   // ... loaded as a supported tcgen05.ld width (the extra columns lie inside
   // the TMEM buffer and are not used)
@@ -159,7 +169,7 @@ struct Cfg {
   static constexpr int kSlots = kSlots0 > kMaxSlots ? kMaxSlots : kSlots0;
   static constexpr int kSmemAlloc = kSlotBase + kSlots * kTileBytes + 1024;
   static constexpr uint32_t kIdescS = idesc_e4m3(128, NS, false, false);
-  static constexpr uint32_t kIdescO = idesc_e4m3(128, NO, true, false);
+  static constexpr uint32_t kIdescO = idesc_e4m3(128, NO, true, kPsTokenMajor);
   static_assert(kSlots >= 2 * kTiles, "ring must hold a K and a V chunk");
   static_assert(kSmemAlloc <= kSmemLimit, "shared memory budget");
   static_assert(kTmemCols <= 512, "TMEM budget");
@@ -307,6 +317,31 @@ __device__ __forceinline__ float warp_max(float x) {
 }
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+// Warp sums of four values at once (butterfly): each step across lane bits
+// 4 and 3 hands half of the remaining values to the partner lane, so the
+// four sums take 6 shuffles instead of 20. Returns the sum of value
+// 2 * (lane bit 4) + (lane bit 3), in every lane that has those bits.
+__device__ __forceinline__ float warp_sum4(const float (&v)[4], int lane) {
+  const bool b4 = (lane & 16) != 0, b3 = (lane & 8) != 0;
+  float s0 = b4 ? v[2] : v[0], s1 = b4 ? v[3] : v[1];
+  const float g0 = b4 ? v[0] : v[2], g1 = b4 ? v[1] : v[3];
+  s0 += __shfl_xor_sync(0xffffffffu, g0, 16);
+  s1 += __shfl_xor_sync(0xffffffffu, g1, 16);
+  float t = b3 ? s1 : s0;
+  t += __shfl_xor_sync(0xffffffffu, b3 ? s0 : s1, 8);
+  t += __shfl_xor_sync(0xffffffffu, t, 4);
+  t += __shfl_xor_sync(0xffffffffu, t, 2);
+  t += __shfl_xor_sync(0xffffffffu, t, 1);
+  return t;
+}
+
+// 2^x with the MUFU approximation (a relative error of a few ulp; 2^-inf = 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(r) : "f"(x));
+  return r;
 }
 
 // Bounded wait that also gives up once another role raised the abort flag.
@@ -704,7 +739,11 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < kTile / 32; ++kk) {
               const uint64_t ad = smem_desc_sw128(a0 + kk * 32 * 128, kTileBytes, 1024);
-              const uint64_t bd = smem_desc_sw128(b0 + kk * 32, 16, 1024);
+              // Ps: term-major, 128-byte swizzle (K step: 32 bytes of each
+              // row); token-major: 16-byte columns of 128 tokens, 2048 bytes
+              // apart (K step: 32 tokens of 16 bytes)
+              const uint64_t bd = C::kPsTokenMajor ? smem_desc_mn_interleave(b0 + kk * 32 * 16, 128, 2048)
+                                                   : smem_desc_sw128(b0 + kk * 32, 16, 1024);
               mma_f8(d, ad, bd, C::kIdescO, (!first || kk > 0) ? 1u : 0u);
             }
             first = false;
@@ -751,7 +790,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       tc_fence_after();
       // the O columns of this warp's heads (their kTermsP terms each)
       float v[C::kHeadColsLd];
-      tmem_ld_wait<C::kHeadColsLd>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + h0 * kTermsP, v);
+      tmem_ld_wait<C::kHeadColsLd>(tmem + lane_base + tb * C::kBufCols + C::kTiles * C::NS + half * C::kSetN, v);
       tc_fence_before();
       mbar_arrive(tmem_empty + tb);
 #pragma unroll
@@ -875,41 +914,104 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       }
       named_bar_sync(set_bar, 128);
       if (q4 == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // row table and scales read
+      if constexpr (G >= 8) {
+        // large groups, whose softmax bounds the kernel: the MUFU 2^x, and for
+        // four heads a set the sums in one butterfly (lanes 0, 8, 16, 24 end
+        // with heads 0..3); other counts reduce head by head
+        float psum[4];
 #pragma unroll
-      for (int hh = 0; hh < kSH; ++hh) {
-        float mx = rmax[hh];
+        for (int hh = 0; hh < kSH; ++hh) {
+          float mx = rmax[hh];
 #pragma unroll
-        for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * C::GP + hh]);
-        float sum = 0.f;
+          for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * C::GP + hh]);
+          // a head with no valid entry (mx = -inf) keeps p = 2^-inf = 0
+          if (mx == -INFINITY) mx = 0.f;
+          float sum = 0.f;
 #pragma unroll
-        for (int j = 0; j < C::kTiles; ++j) {
-          const float pr = sc[j][hh] == -INFINITY ? 0.f : exp2f(sc[j][hh] - mx);
-          sc[j][hh] = pr;
-          sum += pr;
+          for (int j = 0; j < C::kTiles; ++j) {
+            const float pr = ex2_approx(sc[j][hh] - mx);
+            sc[j][hh] = pr;
+            sum += pr;
+          }
+          if constexpr (kSH == 4) {
+            psum[hh] = sum;
+          } else {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) rsum[q4 * C::GP + hh] = sum;
+          }
         }
+        if constexpr (kSH == 4) {
+          const float sum = warp_sum4(psum, lane);
+          if ((lane & 7) == 0) rsum[q4 * C::GP + (lane >> 3)] = sum;
+        }
+      } else {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) rsum[q4 * C::GP + hh] = sum;
+        for (int hh = 0; hh < kSH; ++hh) {
+          float mx = rmax[hh];
+#pragma unroll
+          for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * C::GP + hh]);
+          float sum = 0.f;
+#pragma unroll
+          for (int j = 0; j < C::kTiles; ++j) {
+            const float pr = sc[j][hh] == -INFINITY ? 0.f : exp2f(sc[j][hh] - mx);
+            sc[j][hh] = pr;
+            sum += pr;
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          if (lane == 0) rsum[q4 * C::GP + hh] = sum;
+        }
       }
       // probabilities -> FP8 terms of p*256 (row h*kTermsP+t of Ps, one byte per
       // token), two heads per conversion
       uint8_t* ps = smem + C::kPs + pb * C::kPsBytes;
+      if constexpr (C::kPsTokenMajor) {
+        // the set's 16-byte columns of this token: column c holds heads
+        // 4c..4c+3 of the set, 4 terms each (heads past the set's are zero)
 #pragma unroll
-      for (int j = 0; j < C::kTiles; ++j) {
-        if ((mask >> j) & 1u) {
-          uint8_t* pt = ps + j * C::NO * 128;
+        for (int j = 0; j < C::kTiles; ++j) {
+          if ((mask >> j) & 1u) {
+            uint8_t* pt = ps + j * C::NO * 128 + half * (C::kSetN / 16) * 2048 + tk * 16;
 #pragma unroll
-          for (int hh = 0; hh < kSH; hh += 2) {
-            uint16_t tt[kTermsP];
-            split_p2(sc[j][hh] * 256.0f, hh + 1 < kSH ? sc[j][hh + 1] * 256.0f : 0.f, tt);
+            for (int c = 0; c < C::kSetN / 16; ++c) {
+              uint32_t w[4];
 #pragma unroll
-            for (int t = 0; t < kTermsP; ++t) {
-              pt[sw128_offset((h0 + hh) * kTermsP + t, tk)] = (uint8_t)(tt[t] & 0xffu);
-              if (hh + 1 < kSH) pt[sw128_offset((h0 + hh + 1) * kTermsP + t, tk)] = (uint8_t)(tt[t] >> 8);
+              for (int q = 0; q < 4; q += 2) {
+                const int hh = 4 * c + q;
+                if (hh < kSH) {
+                  uint16_t tt[kTermsP];
+                  split_p2(sc[j][hh] * 256.0f, hh + 1 < kSH ? sc[j][hh + 1] * 256.0f : 0.f, tt);
+                  const uint32_t a = (uint32_t)tt[0] | ((uint32_t)tt[1] << 16);
+                  const uint32_t b = (uint32_t)tt[2] | ((uint32_t)tt[3] << 16);
+                  w[q] = __byte_perm(a, b, 0x6420);      // head hh: terms 0..3
+                  w[q + 1] = __byte_perm(a, b, 0x7531);  // head hh + 1
+                } else {
+                  w[q] = w[q + 1] = 0u;
+                }
+              }
+              *reinterpret_cast<uint4*>(pt + c * 2048) = make_uint4(w[0], w[1], w[2], w[3]);
             }
           }
-          if (half == 0)
-            for (int r = C::GP * kTermsP; r < C::NO; ++r) pt[sw128_offset(r, tk)] = 0;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < C::kTiles; ++j) {
+          if ((mask >> j) & 1u) {
+            uint8_t* pt = ps + j * C::NO * 128;
+#pragma unroll
+            for (int hh = 0; hh < kSH; hh += 2) {
+              uint16_t tt[kTermsP];
+              split_p2(sc[j][hh] * 256.0f, hh + 1 < kSH ? sc[j][hh + 1] * 256.0f : 0.f, tt);
+#pragma unroll
+              for (int t = 0; t < kTermsP; ++t) {
+                pt[sw128_offset((h0 + hh) * kTermsP + t, tk)] = (uint8_t)(tt[t] & 0xffu);
+                if (hh + 1 < kSH) pt[sw128_offset((h0 + hh + 1) * kTermsP + t, tk)] = (uint8_t)(tt[t] >> 8);
+              }
+            }
+            if (half == 0)
+              for (int r = C::GP * kTermsP; r < C::NO; ++r) pt[sw128_offset(r, tk)] = 0;
+          }
         }
       }
       fence_proxy_async_smem();
