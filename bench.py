@@ -8,8 +8,10 @@ d128, page 16, 32 pages/request, Top-K 512 = every token in random order) on
 every GPU -- one process per GPU under torchrun, requests sharded by rank
 with no data-path collective, so per-GPU work is fixed ("weak" scaling; at 8
 GPUs the job is configs[3]'s 2048 requests). A step is one decode call over
-the rank's batch with all inputs resident in HBM; L2 is flushed (a 256 MiB
-write) between timed steps, outside the timed events.
+the rank's batch with all inputs resident in HBM; L2 is flushed between timed
+steps, outside the timed events: a 256 MiB write, then a 256 MiB read, so
+that the write's dirty lines go back to HBM before the next step instead of
+during it (``us_per_call_write_flush`` reports the write-only flush).
 
 Reported ``value``: achieved HBM TB/s on unique FP8 K/V bytes summed over
 ranks / max-over-ranks device time per call (the north star's figure);
@@ -44,6 +46,27 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "µs/call + achieved HBM TB/s (vs ~8 TB/s) @256 req, TopK 512; 1/2/4/8 GPU"
 FLUSH_BYTES = 256 << 20
+L2_NOTE = ("flushed between timed steps, outside the timed events: 256 MiB written, then 256 MiB read so the "
+           "written lines are back in HBM before the step")
+
+
+class L2Flush:
+    """Flush of the 126 MB L2 between timed steps: a write of FLUSH_BYTES
+    evicts every input line, and a read of another FLUSH_BYTES then evicts
+    the write's dirty lines, whose write-back would otherwise share HBM with
+    the next timed step (the write-only flush is kept for comparison)."""
+
+    def __init__(self, dev):
+        import torch
+
+        self.w = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+
+    def __call__(self, write_only: bool = False):
+        self.w.zero_()
+        if not write_only:
+            self.r.max()
+
 FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch on
@@ -314,7 +337,7 @@ def run_ours(args):
 
     w = make_workload(args.config, dev, seed=0, shard=rank)
     acct = kv_bytes(w)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     out = torch.empty_like(w.q)
     kernel = args.kernel
     # tensor-core path: the row-map kernel and the decode kernel (+ the split
@@ -330,7 +353,7 @@ def run_ours(args):
     # ---- device-resident timing --------------------------------------------
     for _ in range(max(3, args.warmup)):
         call()
-        flush.zero_()
+        flush()
     stream = torch.cuda.current_stream()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -343,10 +366,19 @@ def run_ours(args):
             starts[i].record(stream)
             call()
             ends[i].record(stream)
-            flush.zero_()
+            flush()
         region1.record(stream)
         barrier(world, local)
     kern_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    # the same steps after a write-only flush, for comparison: the flush's
+    # dirty lines then go back to HBM during the step
+    for i in range(args.steps):
+        starts[i].record(stream)
+        call()
+        ends[i].record(stream)
+        flush(write_only=True)
+    barrier(world, local)
+    wf_ms = reduce_max(sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps, world, local)
     local_ms = sum(kern_ms) / len(kern_ms)
     step_ms = reduce_max(local_ms, world, local)
     total_unique = reduce_sum(acct["unique_kv"], world, local)
@@ -437,8 +469,9 @@ def run_ours(args):
             "config": {"workload": workload_name(args.config), "rows_per_gpu": w.rows, "rows_total": w.rows * world,
                        "hq": w.meta["hq"], "hkv": w.meta["hkv"], "head_dim": 128, "page": w.meta["page"],
                        "pages_per_req": w.meta["ppr"], "topk": w.meta["topk"], "kernel": kernel,
-                       "l2": "flushed between timed steps (256 MiB write, outside the timed events)",
+                       "l2": L2_NOTE,
                        "parallelism": f"request-sharded x{world}, no collective"},
+            "us_per_call_write_flush": wf_ms * 1e3,
             "bytes_per_gpu": {"unique_kv": acct["unique_kv"], "logical_kv": acct["logical_kv"],
                               "algorithmic": acct["algorithmic"]},
             "logical_kv_tbs": total_logical / (step_ms * 1e-3) / 1e12,
@@ -490,14 +523,14 @@ def run_cache_write(args):
     v_new = torch.randn(tokens, hkv, 128, generator=gen, device=dev).to(torch.bfloat16)
     kc = torch.empty(npages, page, hkv, 128, dtype=torch.float8_e4m3fn, device=dev)
     vc = torch.empty_like(kc)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
 
     def call():
         qsa_b200.qsa_cache_write(k_new, v_new, slots, 0.05, 0.05, kc, vc)
 
     for _ in range(max(3, args.warmup)):
         call()
-        flush.zero_()
+        flush()
     stream = torch.cuda.current_stream()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -507,7 +540,7 @@ def run_cache_write(args):
             starts[i].record(stream)
             call()
             ends[i].record(stream)
-            flush.zero_()
+            flush()
         torch.cuda.synchronize()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
     moved = tokens * hkv * 128 * (2 * 2 + 2 * 1) + tokens * 8  # bf16 K+V in, e4m3 K+V out, int64 slots
@@ -519,7 +552,7 @@ def run_cache_write(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, e4m3fn out",
         "data": "synthetic",
         "config": {"workload": f"cache write of {workload_name(args.config)}", "tokens": tokens, "hkv": hkv,
-                   "page": page, "l2": "flushed between timed steps (256 MiB write, outside the timed events)"},
+                   "page": page, "l2": L2_NOTE},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                      "peak_source": peak_kind, "traffic": NCU_TRAFFIC_BYTES.get(("cache write", args.config)),
                      "kernel": "qsa_cache_write_kernel",
