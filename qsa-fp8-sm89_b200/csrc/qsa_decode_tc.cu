@@ -45,9 +45,8 @@
 //                      G >= 5 two independent sets, each taking half of the
 //                      heads (odd G padded by one head) with its own named
 //                      barrier: softmax over the chunk's scores (exact max and
-//                      sum), probabilities as FP8 terms of p*256 (operand Ps:
-//                      term-major, one byte per store, for G < 8; token-major,
-//                      16 bytes per store, for G >= 8);
+//                      sum), probabilities as FP8 terms of p*256 (operand Ps,
+//                      token-major: 16 bytes per store);
 //                      then the epilogue of the previous item (its O is
 //                      complete by then): recombine, normalise, v_scale,
 //                      sigmoid gate, bf16 store (or a partial for the split
@@ -118,15 +117,12 @@ struct Cfg {
   static_assert(kThreads % 128 == 0, "whole warpgroups, so the four sub-partitions hold equal shares");
   static constexpr int NS = ((G * kTermsQ + 15) / 16) * 16;  // N of the S MMA (rows of Qs)
   static constexpr int kHalfHeads = GP / kSoftmaxSets;       // heads of one softmax set
-  // Ps of the large groups is token-major (the MN-major B operand of the O
-  // MMA): each token's probability terms are contiguous, so a thread stores
-  // its set's terms of a tile in 16-byte pieces, and each set's heads are
-  // padded to whole 16-byte columns (4 heads x 4 terms). Small groups keep
-  // Ps term-major (K-major, 128-byte swizzle), one byte per store.
-  static constexpr bool kPsTokenMajor = G >= 8;
-  static constexpr int kSetN = kPsTokenMajor ? ((kHalfHeads * kTermsP + 15) / 16) * 16 : kHalfHeads * kTermsP;
-  static constexpr int NO = kPsTokenMajor ? kSoftmaxSets * kSetN
-                                          : ((G * kTermsP + 15) / 16) * 16;  // N of the O MMA (terms of a Ps tile)
+  // Ps is token-major (the MN-major B operand of the O MMA): each token's
+  // probability terms are contiguous, so a thread stores its set's terms of
+  // a tile in 16-byte pieces, and each set's heads are padded to whole
+  // 16-byte columns (4 heads x 4 terms)
+  static constexpr int kSetN = ((kHalfHeads * kTermsP + 15) / 16) * 16;  // O columns of one set
+  static constexpr int NO = kSoftmaxSets * kSetN;  // N of the O MMA (terms of a Ps tile)
   static constexpr int kTiles = 4;                          // tiles per item
   static constexpr int kChunk = kTiles * kTile;             // Top-K entries per item
   static constexpr int kBufCols = (kTiles * NS + NO + 31) / 32 * 32;  // S tiles + O, per TMEM buffer
@@ -169,7 +165,7 @@ struct Cfg {
   static constexpr int kSlots = kSlots0 > kMaxSlots ? kMaxSlots : kSlots0;
   static constexpr int kSmemAlloc = kSlotBase + kSlots * kTileBytes + 1024;
   static constexpr uint32_t kIdescS = idesc_e4m3(128, NS, false, false);
-  static constexpr uint32_t kIdescO = idesc_e4m3(128, NO, true, kPsTokenMajor);
+  static constexpr uint32_t kIdescO = idesc_e4m3(128, NO, true, true);
   static_assert(kSlots >= 2 * kTiles, "ring must hold a K and a V chunk");
   static_assert(kSmemAlloc <= kSmemLimit, "shared memory budget");
   static_assert(kTmemCols <= 512, "TMEM budget");
@@ -739,11 +735,9 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < kTile / 32; ++kk) {
               const uint64_t ad = smem_desc_sw128(a0 + kk * 32 * 128, kTileBytes, 1024);
-              // Ps: term-major, 128-byte swizzle (K step: 32 bytes of each
-              // row); token-major: 16-byte columns of 128 tokens, 2048 bytes
-              // apart (K step: 32 tokens of 16 bytes)
-              const uint64_t bd = C::kPsTokenMajor ? smem_desc_mn_interleave(b0 + kk * 32 * 16, 128, 2048)
-                                                   : smem_desc_sw128(b0 + kk * 32, 16, 1024);
+              // Ps: 16-byte columns of 128 tokens, 2048 bytes apart (K step:
+              // 32 tokens of 16 bytes)
+              const uint64_t bd = smem_desc_mn_interleave(b0 + kk * 32 * 16, 128, 2048);
               mma_f8(d, ad, bd, C::kIdescO, (!first || kk > 0) ? 1u : 0u);
             }
             first = false;
@@ -914,103 +908,63 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       }
       named_bar_sync(set_bar, 128);
       if (q4 == 0 && lane == 0 && !failed) mbar_arrive(meta_empty + m);  // row table and scales read
-      if constexpr (G >= 8) {
-        // large groups, whose softmax bounds the kernel: the MUFU 2^x, and for
-        // four heads a set the sums in one butterfly (lanes 0, 8, 16, 24 end
-        // with heads 0..3); other counts reduce head by head
-        float psum[4];
+      // probabilities by the MUFU 2^x; for four heads a set the sums go through
+      // one butterfly (lanes 0, 8, 16, 24 end with heads 0..3), other counts
+      // reduce head by head
+      float psum[4];
 #pragma unroll
-        for (int hh = 0; hh < kSH; ++hh) {
-          float mx = rmax[hh];
+      for (int hh = 0; hh < kSH; ++hh) {
+        float mx = rmax[hh];
 #pragma unroll
-          for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * C::GP + hh]);
-          // a head with no valid entry (mx = -inf) keeps p = 2^-inf = 0
-          if (mx == -INFINITY) mx = 0.f;
-          float sum = 0.f;
+        for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * C::GP + hh]);
+        // a head with no valid entry (mx = -inf) keeps p = 2^-inf = 0
+        if (mx == -INFINITY) mx = 0.f;
+        float sum = 0.f;
 #pragma unroll
-          for (int j = 0; j < C::kTiles; ++j) {
-            const float pr = ex2_approx(sc[j][hh] - mx);
-            sc[j][hh] = pr;
-            sum += pr;
-          }
-          if constexpr (kSH == 4) {
-            psum[hh] = sum;
-          } else {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) rsum[q4 * C::GP + hh] = sum;
-          }
+        for (int j = 0; j < C::kTiles; ++j) {
+          const float pr = ex2_approx(sc[j][hh] - mx);
+          sc[j][hh] = pr;
+          sum += pr;
         }
         if constexpr (kSH == 4) {
-          const float sum = warp_sum4(psum, lane);
-          if ((lane & 7) == 0) rsum[q4 * C::GP + (lane >> 3)] = sum;
-        }
-      } else {
-#pragma unroll
-        for (int hh = 0; hh < kSH; ++hh) {
-          float mx = rmax[hh];
-#pragma unroll
-          for (int i = 1; i < 4; ++i) mx = fmaxf(mx, rmax[i * C::GP + hh]);
-          float sum = 0.f;
-#pragma unroll
-          for (int j = 0; j < C::kTiles; ++j) {
-            const float pr = sc[j][hh] == -INFINITY ? 0.f : exp2f(sc[j][hh] - mx);
-            sc[j][hh] = pr;
-            sum += pr;
-          }
+          psum[hh] = sum;
+        } else {
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
           if (lane == 0) rsum[q4 * C::GP + hh] = sum;
         }
       }
+      if constexpr (kSH == 4) {
+        const float sum = warp_sum4(psum, lane);
+        if ((lane & 7) == 0) rsum[q4 * C::GP + (lane >> 3)] = sum;
+      }
       // probabilities -> FP8 terms of p*256 (row h*kTermsP+t of Ps, one byte per
       // token), two heads per conversion
       uint8_t* ps = smem + C::kPs + pb * C::kPsBytes;
-      if constexpr (C::kPsTokenMajor) {
-        // the set's 16-byte columns of this token: column c holds heads
-        // 4c..4c+3 of the set, 4 terms each (heads past the set's are zero)
+      // the set's 16-byte columns of this token: column c holds heads 4c..4c+3
+      // of the set, 4 terms each (heads past the set's are zero)
 #pragma unroll
-        for (int j = 0; j < C::kTiles; ++j) {
-          if ((mask >> j) & 1u) {
-            uint8_t* pt = ps + j * C::NO * 128 + half * (C::kSetN / 16) * 2048 + tk * 16;
+      for (int j = 0; j < C::kTiles; ++j) {
+        if ((mask >> j) & 1u) {
+          uint8_t* pt = ps + j * C::NO * 128 + half * (C::kSetN / 16) * 2048 + tk * 16;
 #pragma unroll
-            for (int c = 0; c < C::kSetN / 16; ++c) {
-              uint32_t w[4];
+          for (int c = 0; c < C::kSetN / 16; ++c) {
+            uint32_t w[4];
 #pragma unroll
-              for (int q = 0; q < 4; q += 2) {
-                const int hh = 4 * c + q;
-                if (hh < kSH) {
-                  uint16_t tt[kTermsP];
-                  split_p2(sc[j][hh] * 256.0f, hh + 1 < kSH ? sc[j][hh + 1] * 256.0f : 0.f, tt);
-                  const uint32_t a = (uint32_t)tt[0] | ((uint32_t)tt[1] << 16);
-                  const uint32_t b = (uint32_t)tt[2] | ((uint32_t)tt[3] << 16);
-                  w[q] = __byte_perm(a, b, 0x6420);      // head hh: terms 0..3
-                  w[q + 1] = __byte_perm(a, b, 0x7531);  // head hh + 1
-                } else {
-                  w[q] = w[q + 1] = 0u;
-                }
-              }
-              *reinterpret_cast<uint4*>(pt + c * 2048) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          }
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < C::kTiles; ++j) {
-          if ((mask >> j) & 1u) {
-            uint8_t* pt = ps + j * C::NO * 128;
-#pragma unroll
-            for (int hh = 0; hh < kSH; hh += 2) {
-              uint16_t tt[kTermsP];
-              split_p2(sc[j][hh] * 256.0f, hh + 1 < kSH ? sc[j][hh + 1] * 256.0f : 0.f, tt);
-#pragma unroll
-              for (int t = 0; t < kTermsP; ++t) {
-                pt[sw128_offset((h0 + hh) * kTermsP + t, tk)] = (uint8_t)(tt[t] & 0xffu);
-                if (hh + 1 < kSH) pt[sw128_offset((h0 + hh + 1) * kTermsP + t, tk)] = (uint8_t)(tt[t] >> 8);
+            for (int q = 0; q < 4; q += 2) {
+              const int hh = 4 * c + q;
+              if (hh < kSH) {
+                uint16_t tt[kTermsP];
+                split_p2(sc[j][hh] * 256.0f, hh + 1 < kSH ? sc[j][hh + 1] * 256.0f : 0.f, tt);
+                const uint32_t a = (uint32_t)tt[0] | ((uint32_t)tt[1] << 16);
+                const uint32_t b = (uint32_t)tt[2] | ((uint32_t)tt[3] << 16);
+                w[q] = __byte_perm(a, b, 0x6420);      // head hh: terms 0..3
+                w[q + 1] = __byte_perm(a, b, 0x7531);  // head hh + 1
+              } else {
+                w[q] = w[q + 1] = 0u;
               }
             }
-            if (half == 0)
-              for (int r = C::GP * kTermsP; r < C::NO; ++r) pt[sw128_offset(r, tk)] = 0;
+            *reinterpret_cast<uint4*>(pt + c * 2048) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
