@@ -72,7 +72,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch on
 # the bench workload, from the ncu capture summarised in profiles/ (None until
 # captured for the current kernel).
-NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): 278_276_864, ("cache write", 1): 772_670_000}
+NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): 278_676_480, ("cache write", 1): 772_670_000}
 
 
 def parse():
