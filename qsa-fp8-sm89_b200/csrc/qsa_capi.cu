@@ -134,6 +134,7 @@ void fill_params(const qsa_b200_decode_args* a, DecodeParams* p) {
   p->rowmap_stride = p->num_chunks * p->chunk_tokens;
   p->tile_flags = nullptr;
   p->item_counter = nullptr;
+  p->merge_chunks = 0;
   p->err = nullptr;
 }
 
@@ -227,7 +228,7 @@ int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t wo
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e = use_tc ? launch_decode_tc(p, s) : launch_decode_simt(p, s);
   if (e != cudaSuccess) return QSA_B200_ERR_LAUNCH;
-  if (p.num_chunks > 1) {
+  if (p.num_chunks > 1 && !(use_tc && tc_merges_chunks(p))) {
     e = launch_combine(p, s);
     if (e != cudaSuccess) return QSA_B200_ERR_LAUNCH;
   }

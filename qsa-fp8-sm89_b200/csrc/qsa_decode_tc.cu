@@ -181,7 +181,13 @@ struct Item {
   int row, g, chunk;
 };
 
+// Published item ids of split rows may carry kLastChunk: the last published
+// chunk of its (row, KV head) when the CTA merges the chunks itself.
+constexpr int kLastChunk = 1 << 30;
+constexpr int kItemMask = kLastChunk - 1;
+
 __device__ __forceinline__ Item item_of(const DecodeParams& p, int item) {
+  item &= kItemMask;
   Item it;
   it.g = item % p.num_kv_heads;
   const int rc = item / p.num_kv_heads;
@@ -191,23 +197,30 @@ __device__ __forceinline__ Item item_of(const DecodeParams& p, int item) {
 }
 
 // The decoder's walk over the items when rows are split (num_chunks > 1).
-// Items are taken in windows of kWalkWindow claim indices. Claim index c
-// stands for (row, chunk) rc = c % (rows * num_chunks) and KV head
-// c / (rows * num_chunks), so a window holds consecutive chunks of one row
-// for one head. A CTA's first window is static (c from blockIdx.x *
-// kWalkWindow); later ones are claimed from the per-call counter, from
-// gridDim.x * kWalkWindow on, so a CTA that draws long rows (or runs slow)
-// takes fewer: ragged rows make the work per window uneven. An item whose
-// chunk holds no valid tile (past a ragged row's end) is left out, never
-// published, and its partials get a log-sum of -inf, which tells the split
-// combine that the chunk is empty. Each window's claim is issued two windows
-// and its tile flags one window before it is walked, so neither wait shows.
+// Items are taken in windows of w claim indices. Claim index c stands for
+// (row, chunk) rc = c % (rows * num_chunks) and KV head c / (rows *
+// num_chunks), so a window holds consecutive chunks of one row for one head.
+// A CTA's first window is static (c from blockIdx.x * w); later ones are
+// claimed from the per-call counter, from gridDim.x * w on, so a CTA that
+// draws long rows (or runs slow) takes fewer: ragged rows make the work per
+// window uneven. An item whose chunk holds no valid tile (past a ragged
+// row's end) is left out and never published. Each window's claim is issued
+// two windows and its tile flags one window before it is walked, so neither
+// wait shows.
+//   Partials (merge_chunks == 0): w = kWalkWindow; a left-out item's
+//     partials get a log-sum of -inf, which tells the split combine that the
+//     chunk is empty.
+//   Merged (merge_chunks == 1): w = num_chunks, so a window is exactly the
+//     chunks of one (row, KV head), published in order; the last one carries
+//     kLastChunk. A window with no valid chunk (a fully masked row) gets its
+//     zero output here.
 constexpr int kWalkWindow = 4;
 struct ItemWalk {
+  int w;                // claim indices per window
   int base;             // first claim index of the current window
   uint32_t live;        // bit b: claim index base + b is still to be published
   int next_base;        // first claim index of the next window
-  uint32_t next_flags;  // lane b < kWalkWindow: tile flags word of claim index next_base + b
+  uint32_t next_flags;  // lane b < w: tile flags word of claim index next_base + b
   int claim;            // lane 0: first claim index of the window after next (in flight)
 };
 
@@ -215,26 +228,27 @@ __device__ __forceinline__ int claim_rc(const DecodeParams& p, int c) { return c
 __device__ __forceinline__ int claim_item(const DecodeParams& p, int c) {
   return claim_rc(p, c) * p.num_kv_heads + c / (p.rows * p.num_chunks);
 }
-__device__ __forceinline__ uint32_t claim_flags(const DecodeParams& p, int c, int num_items, int lane) {
-  return (lane < kWalkWindow && c < num_items)
+__device__ __forceinline__ uint32_t claim_flags(const DecodeParams& p, int w, int c, int num_items, int lane) {
+  return (lane < w && c < num_items)
              ? *reinterpret_cast<const uint32_t*>(p.tile_flags + (int64_t)claim_rc(p, c) * 16)
              : 0u;
 }
-__device__ __forceinline__ int claim_window(const DecodeParams& p) {
-  return (int)gridDim.x * kWalkWindow + atomicAdd(p.item_counter, kWalkWindow);
+__device__ __forceinline__ int claim_window(const DecodeParams& p, int w) {
+  return (int)gridDim.x * w + atomicAdd(p.item_counter, w);
 }
 
 // Must follow griddepcontrol.wait (the flags and the counter come from the
 // row-map kernel).
 __device__ __forceinline__ void walk_init(ItemWalk& wk, const DecodeParams& p, int num_items, int lane) {
+  wk.w = p.merge_chunks ? p.num_chunks : kWalkWindow;
   wk.base = 0;
   wk.live = 0;
-  wk.next_base = (int)blockIdx.x * kWalkWindow;
-  wk.next_flags = claim_flags(p, wk.next_base + lane, num_items, lane);
-  wk.claim = lane == 0 ? claim_window(p) : 0;
+  wk.next_base = (int)blockIdx.x * wk.w;
+  wk.next_flags = claim_flags(p, wk.w, wk.next_base + lane, num_items, lane);
+  wk.claim = lane == 0 ? claim_window(p, wk.w) : 0;
 }
 
-// The next item of the walk, -1 at its end.
+// The next item of the walk (with kLastChunk where it applies), -1 at its end.
 template <int G>
 __device__ __forceinline__ int walk_next(ItemWalk& wk, const DecodeParams& p, int num_items, int lane) {
   while (wk.live == 0u) {
@@ -242,23 +256,33 @@ __device__ __forceinline__ int walk_next(ItemWalk& wk, const DecodeParams& p, in
     // the next window becomes the current one
     wk.base = wk.next_base;
     const int c = wk.base + lane;
-    const bool in = lane < kWalkWindow && c < num_items;
+    const bool in = lane < wk.w && c < num_items;
     const bool keep = in && wk.next_flags != 0u;
     wk.live = __ballot_sync(0xffffffffu, keep);
-    if (in && !keep) {
-      const Item w = item_of(p, claim_item(p, c));
+    if (!p.merge_chunks) {
+      if (in && !keep) {
+        const Item w = item_of(p, claim_item(p, c));
+#pragma unroll 1
+        for (int h = 0; h < G; ++h)
+          p.part_lse[((int64_t)w.row * p.num_q_heads + w.g * G + h) * p.num_chunks + w.chunk] = -INFINITY;
+      }
+    } else if (wk.live == 0u) {
+      // a (row, KV head) without a valid entry: its G heads are zeros
+      const Item w = item_of(p, claim_item(p, wk.base));
 #pragma unroll 1
       for (int h = 0; h < G; ++h)
-        p.part_lse[((int64_t)w.row * p.num_q_heads + w.g * G + h) * p.num_chunks + w.chunk] = -INFINITY;
+        *reinterpret_cast<uint2*>(p.out + ((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim + lane * 4) =
+            make_uint2(0u, 0u);
     }
     // the window after it (claimed one window ago) and a claim for the one after that
     wk.next_base = __shfl_sync(0xffffffffu, wk.claim, 0);
-    wk.next_flags = claim_flags(p, wk.next_base + lane, num_items, lane);
-    if (lane == 0 && wk.next_base < num_items) wk.claim = claim_window(p);
+    wk.next_flags = claim_flags(p, wk.w, wk.next_base + lane, num_items, lane);
+    if (lane == 0 && wk.next_base < num_items) wk.claim = claim_window(p, wk.w);
   }
   const int b = __ffs(wk.live) - 1;
   wk.live &= wk.live - 1u;
-  return claim_item(p, wk.base + b);
+  const int item = claim_item(p, wk.base + b);
+  return (p.merge_chunks && wk.live == 0u) ? (item | kLastChunk) : item;
 }
 
 // Named-barrier vote of count threads: true when pred holds in any of them.
@@ -483,7 +507,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
   if (warp == kDecoderWarp) {
     // =============================== decoder ================================
     auto load_q = [&](int item, uint2 (&q)[G]) {
-      if (item < num_items) {
+      if ((item & kItemMask) < num_items) {
         const Item w = item_of(p, item);
 #pragma unroll
         for (int h = 0; h < G; ++h)
@@ -503,7 +527,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     if (split) {
       walk_init(wk, p, num_items, lane);
       nx = walk_next<G>(wk, p, num_items, lane);
-      if (nx >= 0 && nx != item_at(0)) load_q(nx, q_n);
+      if (nx >= 0 && (nx & kItemMask) != item_at(0)) load_q(nx, q_n);
     }
     int k = 0;  // published items so far
     for (;; ++k) {
@@ -774,8 +798,19 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     // state of the item whose epilogue is pending
     int e_k = -1, e_row = 0, e_g = 0, e_chunk = 0;
     bool e_any = false;  // the pending item has a valid tile
+    bool e_last = false;  // merged split rows: the pending item ends its (row, KV head)
     float e_m[C::kHalfHeads], e_l[C::kHalfHeads];
     __nv_bfloat16 e_gate[C::kHalfHeads];
+    // merged split rows: the running merge of the current (row, KV head)'s
+    // chunks, per head (unnormalised output of dim tk, its log2 maximum and
+    // sum), the flash-decoding combine done in registers
+    float mg_u[C::kHalfHeads], mg_m[C::kHalfHeads], mg_l[C::kHalfHeads];
+#pragma unroll
+    for (int hh = 0; hh < C::kHalfHeads; ++hh) {
+      mg_u[hh] = 0.f;
+      mg_m[hh] = -INFINITY;
+      mg_l[hh] = 0.f;
+    }
     auto epilogue = [&]() {
       const int tb = e_k % C::kTmemBufs;
       if (!failed)
@@ -804,6 +839,28 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
           const float sig = __fdividef(1.0f, 1.0f + __expf(fminf(-gt, 80.0f)));
           p.out[hrow * kHeadDim + tk] = __float2bfloat16_rn(o * p.v_scale * sig);
         } else {
+          if constexpr (split && G <= 8) {  // (tc_merges_chunks holds only for G <= 8)
+            if (p.merge_chunks) {
+              if (e_any && e_l[hh] > 0.f) {
+                const float u = combine_p(v + hh * kTermsP) * (1.0f / 256.0f);
+                const float mn = fmaxf(mg_m[hh], e_m[hh]);
+                const float a = ex2_approx(mg_m[hh] - mn), b = ex2_approx(e_m[hh] - mn);
+                mg_u[hh] = mg_u[hh] * a + u * b;
+                mg_l[hh] = mg_l[hh] * a + e_l[hh] * b;
+                mg_m[hh] = mn;
+              }
+              if (e_last) {  // the (row, KV head)'s last chunk: normalise, gate, store
+                const float gt = __bfloat162float(e_gate[hh]);
+                const float sig = __fdividef(1.0f, 1.0f + __expf(fminf(-gt, 80.0f)));
+                const float om = mg_l[hh] > 0.f ? __fdividef(mg_u[hh], mg_l[hh]) : 0.f;
+                p.out[hrow * kHeadDim + tk] = __float2bfloat16_rn(om * p.v_scale * sig);
+                mg_u[hh] = 0.f;
+                mg_m[hh] = -INFINITY;
+                mg_l[hh] = 0.f;
+              }
+              continue;
+            }
+          }
           const int64_t pidx = hrow * p.num_chunks + e_chunk;
           p.part_o[pidx * kHeadDim + tk] = o;
           if (tk == 0) p.part_lse[pidx] = e_l[hh] > 0.f ? e_m[hh] + log2f(e_l[hh]) : -INFINITY;
@@ -836,7 +893,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       const Item w = item_of(p, split ? li : item_at(li));
       // the gate of this warp's heads, needed by the epilogue one iteration later
       __nv_bfloat16 gate[C::kHalfHeads];
-      if (p.num_chunks == 1) {
+      if (split ? p.merge_chunks != 0 : p.num_chunks == 1) {
 #pragma unroll
         for (int hh = 0; hh < C::kHalfHeads; ++hh)
           gate[hh] = h0 + hh < G ? p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h0 + hh) * kHeadDim + tk]
@@ -978,6 +1035,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       e_row = w.row;
       e_g = w.g;
       e_chunk = w.chunk;
+      if constexpr (split) e_last = (li & kLastChunk) != 0;
       e_any = mask != 0;
 #pragma unroll
       for (int hh = 0; hh < C::kHalfHeads; ++hh) {
@@ -993,7 +1051,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         }
         e_m[hh] = mx;
         e_l[hh] = l;
-        e_gate[hh] = p.num_chunks == 1 ? gate[hh] : __float2bfloat16_rn(0.f);
+        e_gate[hh] = (split ? p.merge_chunks != 0 : p.num_chunks == 1) ? gate[hh] : __float2bfloat16_rn(0.f);
       }
     }
     if (e_k >= 0) epilogue();
@@ -1176,7 +1234,20 @@ bool tc_supports_group(int group) {
   return (group >= 1 && group <= 8) || (group <= 16 && group % 2 == 0);
 }
 
-cudaError_t launch_decode_tc(const DecodeParams& p, cudaStream_t stream) {
+// Split rows merge in the CTA when there are enough (row, KV head) pairs to
+// share out (at least two per SM), the chunks fit a warp's ballot, and the
+// group leaves the softmax warps room for the merge registers; otherwise the
+// chunks go out as partials to the combine kernel, which also spreads a few
+// long rows over all SMs.
+bool tc_merges_chunks(const DecodeParams& p) {
+  return p.num_chunks > 1 && p.num_chunks <= 32 && p.group <= 8 &&
+         (int64_t)p.rows * p.num_kv_heads >= 2 * (int64_t)sm_count() &&
+         (int64_t)p.rows * p.num_kv_heads * p.num_chunks < kLastChunk;
+}
+
+cudaError_t launch_decode_tc(const DecodeParams& params, cudaStream_t stream) {
+  DecodeParams p = params;
+  p.merge_chunks = tc_merges_chunks(params) ? 1 : 0;
   switch (p.group) {
     case 1: return launch_g<1>(p, stream);
     case 2: return launch_g<2>(p, stream);

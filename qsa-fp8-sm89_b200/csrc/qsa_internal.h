@@ -60,6 +60,10 @@ struct DecodeParams {
   // Claim counter of the tensor-core kernel (workspace, zeroed by its row-map
   // kernel): with split rows, CTAs claim windows of items from it.
   int* item_counter;
+  // Tensor-core kernel, split rows: 1 when each CTA walks all chunks of a
+  // (row, KV head) in turn and merges them itself (no partials, no combine
+  // kernel); set by the launcher from tc_merges_chunks.
+  int merge_chunks;
 
   int* err;  // device error word of the current device
 };
@@ -91,6 +95,9 @@ cudaError_t launch_cache_write(const CacheWriteParams& p, cudaStream_t stream);
 // group sizes of the tensor-core kernel.
 int tc_chunk_tokens(int group);
 bool tc_supports_group(int group);
+// Whether the tensor-core decode merges the chunks of split rows itself, so
+// that the split combine is not launched.
+bool tc_merges_chunks(const DecodeParams& p);
 
 // Largest group size (Hq / Hkv) the tensor-core kernel handles.
 constexpr int kMaxGroupTc = 16;

@@ -367,6 +367,50 @@ def test_split_rows_with_empty_chunks(hq, kernel):
     assert np.all(bits(out)[[2, 4]] == 0)
 
 
+@pytest.mark.parametrize("hq", [32, 64])
+def test_split_rows_merged_in_cta(hq):
+    """Enough (row, KV head) pairs (40 rows x 8) for the tensor-core kernel to
+    merge each pair's chunks itself instead of writing partials for the
+    combine: masked chunks, only the last chunk valid, fully masked rows
+    (zeros written by the walk) and an invalid request id."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=31 + hq, rows=40, hq=hq, hkv=8, ppr=120, topk=1600, mode="sample")
+    idx = w.indices.clone()
+    idx[0, 512:1024] = -1
+    idx[1, :1536] = -1
+    idx[2, :] = -1
+    idx[3, 700:] = -1
+    idx[5, ::2] = -1
+    t2r = w.t2r.clone()
+    t2r[4] = -1
+    out = qsa_decode(w.q, w.k, w.v, 1.0, 1.0, w.btable, t2r, idx, w.gate, kernel="tc")
+    torch.cuda.synchronize()
+    ref = O.attention(bits(w.q), u8(w.k).reshape(w.k.shape), u8(w.v).reshape(w.v.shape), 1.0, 1.0,
+                      w.btable.cpu().numpy(), t2r.cpu().numpy(), idx.cpu().numpy(), bits(w.gate))
+    check_close(bits(out), ref, what=f"merged split/G={hq // 8}")
+    assert max_ulps(bits(out), ref) <= 1.0
+    assert np.all(bits(out)[[2, 4]] == 0)
+
+
+def test_ragged_gqa8_split_merged_in_cta():
+    """configs[4] shape on a 40-request shard: ragged Top-K up to 2048, each
+    (row, KV head)'s chunks merged by the CTA that walks them."""
+    from qsa_b200 import qsa_decode
+    from qsa_b200.inputs import make_workload
+
+    rows = list(range(40))
+    w = make_workload(4, "cuda", seed=0, row_ids=rows)
+    out = qsa_decode(*w.args(), kernel="tc")
+    torch.cuda.synchronize()
+    ref = oracle_subset(w, rows)
+    check_close(bits(out), ref, what="configs[4] 40 rows / merged")
+    assert max_ulps(bits(out), ref) <= 1.0
+    del w, out
+    torch.cuda.empty_cache()
+
+
 def test_cuda_graph_replay_matches_eager():
     from qsa_b200 import qsa_decode
     from qsa_b200.inputs import make_workload
