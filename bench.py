@@ -341,11 +341,13 @@ def run_ours(args):
     out = torch.empty_like(w.q)
     kernel = args.kernel
     # tensor-core path: the row-map kernel and the decode kernel (+ the split
-    # combine for Top-K rows longer than one chunk); CUDA-core path: the decode
-    # kernel (+ combine)
-    chunk = 512 if w.meta["hq"] // w.meta["hkv"] <= 8 else 256
+    # combine for Top-K rows longer than one chunk, unless the decode merges
+    # the chunks itself); CUDA-core path: the decode kernel (+ combine)
+    chunk = ops.chunk_tokens(w.meta["hq"], w.meta["hkv"])
     tc_path = kernel == "tc" or (kernel == "auto" and ops.tc_supports_group(w.meta["hq"] // w.meta["hkv"]))
-    launches_per_call = (2 if tc_path else 1) + (1 if w.meta["topk"] > chunk else 0)
+    merged = tc_path and ops.tc_merges_chunks(w.rows, w.meta["hq"], w.meta["hkv"], w.meta["topk"],
+                                              torch.cuda.get_device_properties(dev).multi_processor_count)
+    launches_per_call = (2 if tc_path else 1) + (1 if w.meta["topk"] > chunk and not merged else 0)
 
     def call():
         qsa_b200.qsa_decode(*w.args(), out=out, kernel=kernel)

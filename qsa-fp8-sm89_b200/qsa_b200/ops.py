@@ -155,6 +155,16 @@ def tc_supports_group(group: int) -> bool:
     return 1 <= group <= 8 or (group <= 16 and group % 2 == 0)
 
 
+def tc_merges_chunks(rows: int, num_q_heads: int, num_kv_heads: int, topk: int, sm_count: int) -> bool:
+    """Whether the tensor-core decode merges the chunks of split rows itself
+    (the rule of tc_merges_chunks in csrc/qsa_decode_tc.cu): more than one
+    chunk but at most 32, a group of at most 8, at least two (row, KV head)
+    pairs per SM. Otherwise split rows go through the combine kernel."""
+    chunks = -(-topk // chunk_tokens(num_q_heads, num_kv_heads))
+    return (1 < chunks <= 32 and num_q_heads // num_kv_heads <= 8 and rows * num_kv_heads >= 2 * sm_count
+            and rows * num_kv_heads * chunks < (1 << 30))
+
+
 def chunk_tokens(num_q_heads, num_kv_heads) -> int:
     """Top-K entries one work item covers: 512 for every group size."""
     return 512

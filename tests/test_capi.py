@@ -161,3 +161,17 @@ def test_product_never_imports_the_oracle():
     assert files
     for path in files:
         assert not pat.search(path.read_text()), path
+
+
+def test_merge_policy_mirror():
+    """The Python mirror of the decode's rule for merging split rows in the
+    CTA: configs[4] (1024 rows, G = 8, 4 chunks) merges; a 12-row shard, a
+    group of 16, a single chunk or more than 32 chunks do not."""
+    from qsa_b200 import ops
+
+    assert ops.tc_merges_chunks(1024, 64, 8, 2048, 148)
+    assert not ops.tc_merges_chunks(12, 64, 8, 2048, 148)
+    assert not ops.tc_merges_chunks(1024, 128, 8, 2048, 148)
+    assert not ops.tc_merges_chunks(1024, 64, 8, 512, 148)
+    assert not ops.tc_merges_chunks(1024, 64, 8, 512 * 33, 148)
+    assert ops.tc_merges_chunks(37, 32, 8, 1600, 148) and not ops.tc_merges_chunks(36, 32, 8, 1600, 148)
