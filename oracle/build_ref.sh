@@ -6,8 +6,8 @@
 #
 # TEST INFRASTRUCTURE ONLY: the GPU comparator tests load it to check the
 # build against the reference's fastest kernel on the same B200. It is built
-# from the reference checkout where it lies (default /root/reference, or
-# $QSA_REFERENCE_DIR); no reference source is copied into this repository.
+# from the reference checkout where it lies ($QSA_REFERENCE_DIR, or the
+# default location below); no reference source is copied into this repository.
 set -euo pipefail
 here="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 ref="${QSA_REFERENCE_DIR:-/root/reference}"

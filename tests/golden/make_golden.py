@@ -1,8 +1,8 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
-Run once in a container that has the reference checkout (default
-``$QSA_REFERENCE_DIR`` or ``/root/reference``) and the ``cutlass`` DSL
-package, which ``sm89_cutedsl`` imports at module level:
+Run once in a container that has the reference checkout (``$QSA_REFERENCE_DIR``
+or the default of ``--reference-dir``) and the ``cutlass`` DSL package, which
+``sm89_cutedsl`` imports at module level:
 
     python tests/golden/make_golden.py [--reference-dir DIR]
 
