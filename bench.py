@@ -1,7 +1,7 @@
 """Benchmark of the sparse paged GQA FP8 decode path (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config 1] [--kernel auto|tc|simt] [--op decode|cache_write]
+                    [--config 1] [--kernel auto|tc|simt] [--op decode|cache_write|topk]
 
 Workload: BASELINE's headline shape, configs[1] (256 requests x 32q/8kv heads x
 d128, page 16, 32 pages/request, Top-K 512 = every token in random order) on
@@ -84,7 +84,7 @@ def parse():
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--kernel", default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", choices=["decode", "cache_write"], default="decode")
+    ap.add_argument("--op", choices=["decode", "cache_write", "topk"], default="decode")
     return ap.parse_args()
 
 
@@ -501,6 +501,56 @@ def run_ours(args):
 
 
 # ------------------------------------------------------------ cache writer --
+def run_topk(args):
+    """One step = one qsa_topk_select over configs[4]'s shape: 1024 rows of
+    32768 fp32 scores, 2048 indices each (scores resident in HBM, L2 flushed
+    between steps)."""
+    import torch
+
+    if args.gpus != 1:
+        raise SystemExit("--op topk runs on one GPU")
+    dev = torch.device("cuda", 0)
+    import qsa_b200
+
+    rows, ctx, k = 1024, 32768, 2048
+    gen = torch.Generator(device=dev).manual_seed(0)
+    scores = torch.randn(rows, ctx, generator=gen, device=dev)
+    out = torch.empty(rows, k, dtype=torch.int32, device=dev)
+    flush = L2Flush(dev)
+    for _ in range(max(3, args.warmup)):
+        qsa_b200.qsa_topk_select(scores, k, out=out)
+        flush()
+    stream = torch.cuda.current_stream()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        for i in range(args.steps):
+            starts[i].record(stream)
+            qsa_b200.qsa_topk_select(scores, k, out=out)
+            ends[i].record(stream)
+            flush()
+        torch.cuda.synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    moved = rows * ctx * 4 + rows * k * 4  # scores read once, indices written
+    gbs = moved / (ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    line = {
+        "metric": "Top-K index producer GB/s (fp32 scores -> int32 indices)", "value": gbs,
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 in, int32 out",
+        "data": "synthetic",
+        "config": {"workload": "Top-K of configs[4]'s shape", "rows": rows, "ctx": ctx, "k": k, "l2": L2_NOTE},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "peak_source": peak_kind, "traffic": None, "kernel": "qsa_topk_kernel",
+                     "bytes_per_step": moved},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_cache_write(args):
     """One step = one qsa_cache_write of the whole configs[1] cache from bf16
     keys and values (inputs resident in HBM, L2 flushed between steps)."""
@@ -572,6 +622,8 @@ def main():
         return run_reference_arm(args)
     if args.op == "cache_write":
         return run_cache_write(args)
+    if args.op == "topk":
+        return run_topk(args)
     return run_ours(args)
 
 

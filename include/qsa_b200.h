@@ -206,6 +206,29 @@ typedef struct qsa_b200_cache_write_args {
  * 16, and 16-byte aligned caches. Asynchronous on `stream`. */
 QSA_B200_API int qsa_b200_cache_write(const qsa_b200_cache_write_args* args, qsa_b200_stream_t stream);
 
+typedef struct qsa_b200_topk_args {
+  const float* scores;    /* [rows, ctx] fp32 per-position scores, row stride score_stride */
+  const int32_t* lengths; /* optional [rows]: valid positions of each row (clamped to [0, ctx]); NULL = ctx */
+  int32_t* out;           /* [rows, k] int32 Top-K indices, row stride out_stride */
+  int32_t rows;
+  int32_t ctx;            /* positions per row, 1 .. QSA_B200_TOPK_MAX_CTX */
+  int32_t k;              /* selections per row, >= 1 */
+  int64_t score_stride;   /* >= ctx */
+  int64_t out_stride;     /* >= k */
+} qsa_b200_topk_args;
+
+#define QSA_B200_TOPK_MAX_CTX (1 << 20)
+
+/* The Top-K index producer, the step before the decode: for each row, the
+ * positions of the k highest scores, in ascending position order, as the
+ * decode's [rows, k] int32 indices. A position t is a candidate when t is
+ * below the row's length and its score is neither NaN nor -inf; at the k-th
+ * score lower positions win; a row with fewer than k candidates is padded
+ * with -1. No reference counterpart: the reference consumes Top-K indices but
+ * does not produce them (sm89_cutedsl.py:72-76 builds sequential ones).
+ * Needs 4-byte aligned scores, lengths and out. Asynchronous on `stream`. */
+QSA_B200_API int qsa_b200_topk_select(const qsa_b200_topk_args* args, qsa_b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -119,6 +119,28 @@ def f32_to_e4m3fn_sat(x: np.ndarray) -> np.ndarray:
     return code
 
 
+def topk_select(scores, k, lengths=None):
+    """The Top-K index producer's rule, the checker of qsa_topk_kernel. The
+    reference has no producer (it consumes indices; sm89_cutedsl.py:72-76
+    builds sequential ones), so this is the rule the library states: per row,
+    the positions of the k highest scores in ascending position order. A
+    position is a candidate when it is below the row's length (clamped to
+    [0, ctx]) and its score is neither NaN nor -inf; at the k-th score lower
+    positions win; fewer than k candidates are padded with -1."""
+    s = np.asarray(scores, dtype=np.float32)
+    rows, ctx = s.shape
+    out = np.full((rows, k), -1, dtype=np.int32)
+    for r in range(rows):
+        n = ctx if lengths is None else min(max(int(lengths[r]), 0), ctx)
+        v = s[r, :n]
+        cand = np.nonzero(~np.isnan(v) & (v != -np.inf))[0]
+        # highest score first, then the lower position (np.lexsort: last key first)
+        order = cand[np.lexsort((cand, -v[cand].astype(np.float64)))]
+        pick = np.sort(order[:k])
+        out[r, :len(pick)] = pick
+    return out
+
+
 def cache_write(k_cache, v_cache, k_new, v_new, slots, k_scale, v_scale):
     """The paged cache producer: new keys / values quantised into the FP8
     caches at physical token slots; returns updated copies of the caches.

@@ -35,7 +35,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden", "--expt-relaxed-constexpr",
               "-Xptxas", "-warn-spills"] + ARCH
 
-CU_SOURCES = ["qsa_capi.cu", "qsa_decode_tc.cu", "qsa_decode_simt.cu", "qsa_noalloc.cu", "qsa_cache_write.cu"]
+CU_SOURCES = ["qsa_capi.cu", "qsa_decode_tc.cu", "qsa_decode_simt.cu", "qsa_noalloc.cu", "qsa_cache_write.cu",
+              "qsa_topk.cu"]
 HEADERS = ["qsa_common.cuh", "qsa_internal.h"]
 
 LIB = PKG / "libqsa_b200.so"

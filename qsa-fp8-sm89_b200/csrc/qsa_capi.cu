@@ -327,6 +327,32 @@ int qsa_b200_cache_write(const qsa_b200_cache_write_args* a, qsa_b200_stream_t s
   return e == cudaSuccess ? QSA_B200_OK : QSA_B200_ERR_LAUNCH;
 }
 
+int qsa_b200_topk_select(const qsa_b200_topk_args* a, qsa_b200_stream_t stream) {
+  if (!a) return QSA_B200_ERR_NULL_POINTER;
+  if (a->rows < 0 || a->ctx < 1 || a->ctx > QSA_B200_TOPK_MAX_CTX || a->score_stride < a->ctx ||
+      a->out_stride < a->k)
+    return QSA_B200_ERR_BAD_SHAPE;
+  if (a->k < 1) return QSA_B200_ERR_BAD_VALUE;
+  if (a->rows == 0) return QSA_B200_OK;
+  if (!a->scores || !a->out) return QSA_B200_ERR_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(a->scores) & 3u) || (reinterpret_cast<uintptr_t>(a->out) & 3u) ||
+      (reinterpret_cast<uintptr_t>(a->lengths) & 3u))
+    return QSA_B200_ERR_MISALIGNED;
+  const int st = check_device();
+  if (st != QSA_B200_OK) return st;
+  TopkParams p;
+  p.scores = a->scores;
+  p.lengths = a->lengths;
+  p.out = a->out;
+  p.rows = a->rows;
+  p.ctx = a->ctx;
+  p.k = a->k;
+  p.score_stride = a->score_stride;
+  p.out_stride = a->out_stride;
+  const cudaError_t e = launch_topk(p, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? QSA_B200_OK : QSA_B200_ERR_LAUNCH;
+}
+
 int qsa_b200_last_status(void) { return t_last_status; }
 
 int qsa_b200_device_error(int clear) {

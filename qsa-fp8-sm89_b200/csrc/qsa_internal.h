@@ -90,6 +90,16 @@ struct CacheWriteParams {
 };
 cudaError_t launch_cache_write(const CacheWriteParams& p, cudaStream_t stream);
 
+// Top-K index producer (qsa_topk.cu).
+struct TopkParams {
+  const float* scores;
+  const int32_t* lengths;  // may be null
+  int32_t* out;
+  int rows, ctx, k;
+  int64_t score_stride, out_stride;
+};
+cudaError_t launch_topk(const TopkParams& p, cudaStream_t stream);
+
 // Top-K entries per work item for a GQA group size (both kernels split rows
 // the same way, so the workspace size depends only on the shape), and the
 // group sizes of the tensor-core kernel.

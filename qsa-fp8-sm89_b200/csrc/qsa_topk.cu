@@ -1,0 +1,167 @@
+// Top-K index producer: the step before the decode path. For each row of a
+// [rows, ctx] fp32 score matrix it writes the positions of the K highest
+// scores, in ascending position order, as the int32 Top-K indices the decode
+// reads (-1 padding). The reference consumes such indices but does not make
+// them (its fixtures are sequential, sm89_cutedsl.py:72-76).
+//
+// Rule: a position t of row r is a candidate when t < len[r] (ctx without
+// lengths) and its score is neither NaN nor -inf. The K candidates with the
+// highest scores are taken; at the K-th score, lower positions win. Fewer
+// than K candidates: all of them, then -1.
+//
+// One CTA of 1024 threads per row. Scores map to order-preserving uint32
+// keys. A radix select over four 8-bit digits (histogram in shared memory,
+// one warp finds the digit that holds the K-th key) gives the threshold key
+// T and how many keys equal to T to take. An ordered compaction (block
+// prefix sums over 1024-position pieces) then writes the selected positions
+// in ascending order. The kernel reads the row's scores five times, from L2
+// after the first pass.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../../include/qsa_b200.h"
+#include "qsa_internal.h"
+
+namespace qsa {
+namespace {
+
+constexpr int kTopkThreads = 1024;
+constexpr int kTopkWarps = kTopkThreads / 32;
+
+// order-preserving key of a score; 0 for a position that is not a candidate
+__device__ __forceinline__ uint32_t score_key(float s) {
+  const uint32_t u = __float_as_uint(s);
+  if (s != s || s == -INFINITY) return 0u;  // NaN or -inf
+  if (s == 0.f) return 0x80000000u;          // -0 and +0 are the same score
+  const uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return k == 0u ? 1u : k;  // 0 is reserved for non-candidates
+}
+
+// exclusive block prefix sum of one value per thread; also returns the total
+__device__ __forceinline__ int block_scan(int v, int* warp_sums, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_sums[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_sums[lane] = w;  // inclusive
+  }
+  __syncthreads();
+  total = warp_sums[kTopkWarps - 1];
+  const int before = (warp > 0 ? warp_sums[warp - 1] : 0) + x - v;
+  __syncthreads();  // warp_sums is reused by the next scan
+  return before;
+}
+
+__global__ void __launch_bounds__(kTopkThreads) qsa_topk_kernel(const TopkParams p) {
+  __shared__ int hist[256];
+  __shared__ int warp_sums[kTopkWarps];
+  __shared__ uint32_t sel_prefix, sel_mask;
+  __shared__ int sel_remaining;
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const float* sc = p.scores + (int64_t)row * p.score_stride;
+  int32_t* out = p.out + (int64_t)row * p.out_stride;
+  int len = p.ctx;
+  if (p.lengths) {
+    const int l = p.lengths[row];
+    len = l < 0 ? 0 : (l > p.ctx ? p.ctx : l);
+  }
+
+  // ---- radix select: the K-th largest candidate key ------------------------
+  if (tid == 0) {
+    sel_prefix = 0u;
+    sel_mask = 0u;
+    sel_remaining = p.k;
+  }
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 256; b += kTopkThreads) hist[b] = 0;
+    __syncthreads();
+    const uint32_t prefix = sel_prefix, mask = sel_mask;
+    for (int t = tid; t < len; t += kTopkThreads) {
+      const uint32_t key = score_key(sc[t]);
+      if (key != 0u && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // digits from 255 down: the first whose running count reaches the
+      // remaining rank holds the K-th key
+      const int need = sel_remaining;
+      int above = 0, digit = -1;
+      for (int base = 255; base >= 0 && digit < 0; base -= 32) {
+        const int d = base - tid;
+        const int c = hist[d];
+        int incl = c;  // count over digits base .. d
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (tid >= o) incl += y;
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, above + incl >= need);
+        if (hit) {
+          const int first = __ffs(hit) - 1;
+          const int excl = __shfl_sync(0xffffffffu, incl - c, first);
+          digit = base - first;
+          above += excl;
+        } else {
+          above += __shfl_sync(0xffffffffu, incl, 31);
+        }
+      }
+      if (tid == 0) {
+        if (digit < 0) {  // fewer than K candidates (possible in the first pass only)
+          sel_remaining = -1;
+        } else {
+          sel_prefix = prefix | ((uint32_t)digit << shift);
+          sel_mask = mask | (255u << shift);
+          sel_remaining = need - above;
+        }
+      }
+    }
+    __syncthreads();
+    if (sel_remaining < 0) break;
+  }
+  // threshold key T; with fewer than K candidates every candidate is taken
+  const bool all = sel_remaining < 0;
+  const uint32_t T = all ? 1u : sel_prefix;
+  const int take_eq = all ? 0x7fffffff : sel_remaining;
+
+  // ---- ordered compaction ---------------------------------------------------
+  int eq_before = 0, sel_before = 0;
+  for (int t0 = 0; t0 < len; t0 += kTopkThreads) {
+    const int t = t0 + tid;
+    const uint32_t key = t < len ? score_key(sc[t]) : 0u;
+    const bool gt = key != 0u && (all || key > T);
+    const bool eq = !all && key == T && key != 0u;
+    int eq_total;
+    const int eq_rank = eq_before + block_scan(eq ? 1 : 0, warp_sums, eq_total);
+    const bool sel = gt || (eq && eq_rank < take_eq);
+    int sel_total;
+    const int pos = sel_before + block_scan(sel ? 1 : 0, warp_sums, sel_total);
+    if (sel && pos < p.k) out[pos] = t;
+    eq_before += eq_total;
+    sel_before += sel_total;
+  }
+  for (int i = sel_before + tid; i < p.k; i += kTopkThreads) out[i] = -1;
+}
+
+}  // namespace
+
+cudaError_t launch_topk(const TopkParams& p, cudaStream_t stream) {
+  if (p.rows <= 0) return cudaSuccess;
+  qsa_topk_kernel<<<(unsigned)p.rows, kTopkThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace qsa

@@ -7,7 +7,7 @@ hand-written sm_100a CUDA kernels behind a C ABI (``include/qsa_b200.h``,
 """
 
 from ._lib import QsaBuildError, load_clib, load_torch_ops
-from .ops import launch, qsa_cache_write, qsa_decode, run, slots, token_slots, workspace_bytes
+from .ops import launch, qsa_cache_write, qsa_decode, qsa_topk_select, run, slots, token_slots, workspace_bytes
 
 __all__ = [
     "QsaBuildError",
@@ -15,6 +15,7 @@ __all__ = [
     "load_clib",
     "load_torch_ops",
     "qsa_cache_write",
+    "qsa_topk_select",
     "qsa_decode",
     "run",
     "slots",

@@ -53,6 +53,7 @@ EXPORTED = (
     "qsa_b200_abi_version",
     "qsa_b200_decode_noalloc",
     "qsa_b200_cache_write",
+    "qsa_b200_topk_select",
 )
 
 
@@ -109,6 +110,21 @@ class CacheWriteArgs(ctypes.Structure):
     ]
 
 
+class TopkArgs(ctypes.Structure):
+    """Mirror of ``qsa_b200_topk_args``."""
+
+    _fields_ = [
+        ("scores", c_void_p),
+        ("lengths", c_void_p),
+        ("out", c_void_p),
+        ("rows", c_int32),
+        ("ctx", c_int32),
+        ("k", c_int32),
+        ("score_stride", c_int64),
+        ("out_stride", c_int64),
+    ]
+
+
 _configured = False
 
 
@@ -138,6 +154,8 @@ def lib() -> ctypes.CDLL:
         L.qsa_b200_decode_noalloc.restype = c_int
         L.qsa_b200_cache_write.argtypes = [ctypes.POINTER(CacheWriteArgs), c_void_p]
         L.qsa_b200_cache_write.restype = c_int
+        L.qsa_b200_topk_select.argtypes = [ctypes.POINTER(TopkArgs), c_void_p]
+        L.qsa_b200_topk_select.restype = c_int
         _configured = True
     return L
 
@@ -240,6 +258,25 @@ def make_cache_write_args(k_new, v_new, slots, k_cache, v_cache, k_scale=1.0, v_
 def cache_write(args: CacheWriteArgs, stream: int = 0) -> int:
     """Calls ``qsa_b200_cache_write``; returns its status."""
     return int(lib().qsa_b200_cache_write(ctypes.byref(args), c_void_p(stream)))
+
+
+def make_topk_args(scores, k, out, lengths=None) -> TopkArgs:
+    """Fills ``qsa_b200_topk_args`` from torch tensors: fp32 ``scores[rows,
+    ctx]`` and int32 ``out[rows, k]`` with unit inner stride, optional int32
+    ``lengths[rows]``. No data is touched."""
+    a = TopkArgs()
+    a.scores = c_void_p(scores.data_ptr())
+    a.lengths = c_void_p(lengths.data_ptr()) if lengths is not None else None
+    a.out = c_void_p(out.data_ptr())
+    a.rows, a.ctx, a.k = scores.shape[0], scores.shape[1], int(k)
+    a.score_stride = scores.stride(0)
+    a.out_stride = out.stride(0)
+    return a
+
+
+def topk_select(args: TopkArgs, stream: int = 0) -> int:
+    """Calls ``qsa_b200_topk_select``; returns its status."""
+    return int(lib().qsa_b200_topk_select(ctypes.byref(args), c_void_p(stream)))
 
 
 def device_error(clear: bool = False) -> int:

@@ -139,6 +139,35 @@ def qsa_cache_write(k_new, v_new, slots, k_scale, v_scale, k_cache, v_cache):
     return k_cache, v_cache
 
 
+def qsa_topk_select(scores, k, lengths=None, out=None):
+    """Top-K indices for the decode from per-position scores: for each row of
+    fp32 ``scores[rows, ctx]``, the positions of the ``k`` highest scores in
+    ascending position order, int32 ``[rows, k]``, asynchronous on the
+    current stream.
+
+    A position is a candidate when it is below the row's ``lengths`` entry
+    (all ``ctx`` positions without ``lengths``) and its score is neither NaN
+    nor -inf. At the k-th score lower positions win; a row with fewer than
+    ``k`` candidates is padded with -1. The result is the ``indices`` argument
+    of ``qsa_decode`` (a position is a logical token index).
+    """
+    from . import capi
+
+    if scores.dtype != torch.float32 or scores.dim() != 2 or scores.stride(1) != 1 or not scores.is_cuda:
+        raise ValueError("scores must be a CUDA float32 [rows, ctx] tensor with unit inner stride")
+    if lengths is not None and (lengths.dtype != torch.int32 or not lengths.is_contiguous()
+                                or lengths.numel() != scores.shape[0]):
+        raise ValueError("lengths must be a contiguous int32 [rows] tensor")
+    if out is None:
+        out = torch.empty(scores.shape[0], int(k), dtype=torch.int32, device=scores.device)
+    elif out.dtype != torch.int32 or out.dim() != 2 or out.stride(1) != 1 or out.shape != (scores.shape[0], int(k)):
+        raise ValueError("out must be an int32 [rows, k] tensor with unit inner stride")
+    st = capi.topk_select(capi.make_topk_args(scores, k, out, lengths), torch.cuda.current_stream().cuda_stream)
+    if st != 0:
+        raise RuntimeError(f"qsa_b200_topk_select failed: {capi.lib().qsa_b200_status_string(st).decode()}")
+    return out
+
+
 def token_slots(btable, reqs, positions, page_size):
     """Physical slot ``btable[req, pos // P] * P + pos % P`` of each (request,
     position) pair, as int64 -- the ``slots`` argument of

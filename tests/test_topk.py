@@ -1,0 +1,109 @@
+"""Top-K index producer: the oracle's rule on hand-made rows (CPU) and the
+CUDA kernel bit-exact against the oracle (GPU), including ties, -inf, NaN,
+row lengths and a decode fed with the produced indices."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import qsa_oracle as O
+
+
+def test_oracle_rule_by_hand():
+    inf, nan = np.inf, np.nan
+    s = np.array([[3, 1, 3, 2, -inf, nan]], dtype=np.float32)
+    assert O.topk_select(s, 3).tolist() == [[0, 2, 3]]
+    assert O.topk_select(s, 5).tolist() == [[0, 1, 2, 3, -1]]
+    assert O.topk_select(s, 3, lengths=[2]).tolist() == [[0, 1, -1]]
+    assert O.topk_select(s, 2, lengths=[0]).tolist() == [[-1, -1]]
+    ties = np.array([[1, 1, 1, 1], [0.0, -0.0, 0.0, -1]], dtype=np.float32)
+    assert O.topk_select(ties, 2).tolist() == [[0, 1], [0, 1]]
+    assert O.topk_select(np.array([[inf, 5, inf]], dtype=np.float32), 2).tolist() == [[0, 2]]
+
+
+def test_c_abi_rejects_bad_arguments():
+    from qsa_b200 import capi
+
+    a = capi.TopkArgs()
+    a.rows, a.ctx, a.k, a.score_stride, a.out_stride = 2, 100, 0, 100, 1
+    assert capi.topk_select(a) == capi.ERR_BAD_VALUE
+    a.k, a.out_stride = 4, 3
+    assert capi.topk_select(a) != 0
+    a.out_stride, a.ctx = 4, 0
+    assert capi.topk_select(a) != 0
+
+
+def _scores(rows, ctx, kind, seed):
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    if kind == "ties":
+        s = torch.randint(0, 8, (rows, ctx), generator=g).float()
+    else:
+        s = torch.randn(rows, ctx, generator=g)
+    if kind == "special":
+        m = torch.rand(rows, ctx, generator=g)
+        s[m < 0.05] = float("-inf")
+        s[(m >= 0.05) & (m < 0.08)] = float("nan")
+        s[(m >= 0.08) & (m < 0.10)] = float("inf")
+        s[(m >= 0.10) & (m < 0.12)] = -0.0
+    return s
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,ctx,k,kind", [
+    (5, 1000, 17, "randn"), (4, 4096, 512, "ties"), (3, 5000, 2048, "special"),
+    (2, 32768, 2048, "randn"), (3, 2048, 2048, "ties"), (6, 300, 1, "special"), (2, 64, 100, "randn"),
+])
+def test_kernel_matches_oracle(rows, ctx, k, kind):
+    import torch
+
+    from qsa_b200 import qsa_topk_select
+
+    s = _scores(rows, ctx, kind, seed=rows * 7 + k)
+    out = qsa_topk_select(s.cuda(), k)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), O.topk_select(s.numpy(), k))
+
+
+@pytest.mark.gpu
+def test_kernel_row_lengths_and_strides():
+    import torch
+
+    from qsa_b200 import qsa_topk_select
+
+    s = _scores(6, 3000, "ties", seed=11)
+    wide = torch.zeros(6, 3100)
+    wide[:, :3000] = s
+    lengths = torch.tensor([0, 1, 700, 3000, 5000, -3], dtype=torch.int32)
+    out = torch.full((6, 300), 77, dtype=torch.int32, device="cuda")
+    qsa_topk_select(wide.cuda()[:, :3000], 300, lengths=lengths.cuda(), out=out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), O.topk_select(s.numpy(), 300, lengths=lengths.numpy()))
+    # two calls in a row give the same answer
+    again = qsa_topk_select(wide.cuda()[:, :3000], 300, lengths=lengths.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(again, out)
+
+
+@pytest.mark.gpu
+def test_produced_indices_feed_the_decode():
+    """Scores -> Top-K indices -> decode, against the oracle's attention over
+    the oracle's indices."""
+    import torch
+
+    from gpu_helpers import bits, check_close, u8
+    from qsa_b200 import qsa_decode, qsa_topk_select
+    from qsa_b200.inputs import make_workload
+
+    w = make_workload(0, "cuda", seed=5, rows=4, ppr=40, topk=640, mode="sample")
+    ctx = 40 * 16
+    s = _scores(4, ctx, "randn", seed=3)
+    idx = qsa_topk_select(s.cuda(), 200)
+    out = qsa_decode(w.q, w.k, w.v, 1.0, 1.0, w.btable, w.t2r, idx, w.gate)
+    torch.cuda.synchronize()
+    ref_idx = O.topk_select(s.numpy(), 200)
+    ref = O.attention(bits(w.q), u8(w.k).reshape(w.k.shape), u8(w.v).reshape(w.v.shape), 1.0, 1.0,
+                      w.btable.cpu().numpy(), w.t2r.cpu().numpy(), ref_idx, bits(w.gate))
+    check_close(bits(out), ref, what="topk -> decode")
