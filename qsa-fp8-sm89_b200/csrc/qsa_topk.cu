@@ -14,8 +14,9 @@
 // one warp finds the digit that holds the K-th key) gives the threshold key
 // T and how many keys equal to T to take. An ordered compaction (block
 // prefix sums over 1024-position pieces) then writes the selected positions
-// in ascending order. The kernel reads the row's scores five times, from L2
-// after the first pass.
+// in ascending order; each thread takes 4 consecutive positions a step, so
+// two block scans cover 4096 positions. The kernel reads the row's scores
+// five times, from L2 after the first pass.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -137,19 +138,37 @@ __global__ void __launch_bounds__(kTopkThreads) qsa_topk_kernel(const TopkParams
   const uint32_t T = all ? 1u : sel_prefix;
   const int take_eq = all ? 0x7fffffff : sel_remaining;
 
-  // ---- ordered compaction ---------------------------------------------------
+  // ---- ordered compaction: 4 consecutive positions a thread, 4096 a step ----
   int eq_before = 0, sel_before = 0;
-  for (int t0 = 0; t0 < len; t0 += kTopkThreads) {
-    const int t = t0 + tid;
-    const uint32_t key = t < len ? score_key(sc[t]) : 0u;
-    const bool gt = key != 0u && (all || key > T);
-    const bool eq = !all && key == T && key != 0u;
+  for (int t0 = 0; t0 < len; t0 += 4 * kTopkThreads) {
+    const int tb = t0 + 4 * tid;
+    bool gt[4], eq[4];
+    int n_eq = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t key = tb + u < len ? score_key(sc[tb + u]) : 0u;
+      gt[u] = key != 0u && (all || key > T);
+      eq[u] = !all && key == T && key != 0u;
+      n_eq += eq[u] ? 1 : 0;
+    }
     int eq_total;
-    const int eq_rank = eq_before + block_scan(eq ? 1 : 0, warp_sums, eq_total);
-    const bool sel = gt || (eq && eq_rank < take_eq);
+    int eq_rank = eq_before + block_scan(n_eq, warp_sums, eq_total);
+    bool sel[4];
+    int n_sel = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      sel[u] = gt[u] || (eq[u] && eq_rank < take_eq);
+      eq_rank += eq[u] ? 1 : 0;
+      n_sel += sel[u] ? 1 : 0;
+    }
     int sel_total;
-    const int pos = sel_before + block_scan(sel ? 1 : 0, warp_sums, sel_total);
-    if (sel && pos < p.k) out[pos] = t;
+    int pos = sel_before + block_scan(n_sel, warp_sums, sel_total);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (sel[u]) {
+        if (pos < p.k) out[pos] = tb + u;
+        ++pos;
+      }
     eq_before += eq_total;
     sel_before += sel_total;
   }
