@@ -10,13 +10,14 @@
 // than K candidates: all of them, then -1.
 //
 // One CTA of 1024 threads per row. Scores map to order-preserving uint32
-// keys. A radix select over four 8-bit digits (histogram in shared memory,
-// one warp finds the digit that holds the K-th key) gives the threshold key
+// keys. A radix select over three digits of 11, 11 and 10 bits (histogram in
+// shared memory; a block prefix sum over the bins finds the digit that holds
+// the K-th key) gives the threshold key
 // T and how many keys equal to T to take. An ordered compaction (block
 // prefix sums over 1024-position pieces) then writes the selected positions
 // in ascending order; each thread takes 4 consecutive positions a step, so
 // two block scans cover 4096 positions. The kernel reads the row's scores
-// five times, from L2 after the first pass.
+// four times, from L2 after the first pass.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -67,7 +68,7 @@ __device__ __forceinline__ int block_scan(int v, int* warp_sums, int& total) {
 }
 
 __global__ void __launch_bounds__(kTopkThreads) qsa_topk_kernel(const TopkParams p) {
-  __shared__ int hist[256];
+  __shared__ int hist[2048];
   __shared__ int warp_sums[kTopkWarps];
   __shared__ uint32_t sel_prefix, sel_mask;
   __shared__ int sel_remaining;
@@ -82,54 +83,40 @@ __global__ void __launch_bounds__(kTopkThreads) qsa_topk_kernel(const TopkParams
   }
 
   // ---- radix select: the K-th largest candidate key ------------------------
+  // three digits of 11, 11 and 10 bits
   if (tid == 0) {
     sel_prefix = 0u;
     sel_mask = 0u;
     sel_remaining = p.k;
   }
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = tid; b < 256; b += kTopkThreads) hist[b] = 0;
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+    const int nb = pass == 2 ? 1024 : 2048;
+    const uint32_t dmask = (uint32_t)nb - 1u;
+    for (int b = tid; b < 2048; b += kTopkThreads) hist[b] = 0;
     __syncthreads();
     const uint32_t prefix = sel_prefix, mask = sel_mask;
+    const int need = sel_remaining;
     for (int t = tid; t < len; t += kTopkThreads) {
       const uint32_t key = score_key(sc[t]);
-      if (key != 0u && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+      if (key != 0u && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & dmask], 1);
     }
     __syncthreads();
-    if (tid < 32) {
-      // digits from 255 down: the first whose running count reaches the
-      // remaining rank holds the K-th key
-      const int need = sel_remaining;
-      int above = 0, digit = -1;
-      for (int base = 255; base >= 0 && digit < 0; base -= 32) {
-        const int d = base - tid;
-        const int c = hist[d];
-        int incl = c;  // count over digits base .. d
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (tid >= o) incl += y;
-        }
-        const unsigned hit = __ballot_sync(0xffffffffu, above + incl >= need);
-        if (hit) {
-          const int first = __ffs(hit) - 1;
-          const int excl = __shfl_sync(0xffffffffu, incl - c, first);
-          digit = base - first;
-          above += excl;
-        } else {
-          above += __shfl_sync(0xffffffffu, incl, 31);
-        }
-      }
-      if (tid == 0) {
-        if (digit < 0) {  // fewer than K candidates (possible in the first pass only)
-          sel_remaining = -1;
-        } else {
-          sel_prefix = prefix | ((uint32_t)digit << shift);
-          sel_mask = mask | (255u << shift);
-          sel_remaining = need - above;
-        }
-      }
+    // digits from the top: thread tid owns digits nb-1-2*tid and nb-2-2*tid; a
+    // block prefix sum gives the count above each pair, and the thread whose
+    // pair reaches the remaining rank records the digit
+    const int d0 = nb - 1 - 2 * tid, d1 = d0 - 1;
+    const int c0 = d0 >= 0 ? hist[d0] : 0, c1 = d1 >= 0 ? hist[d1] : 0;
+    int total;
+    const int before = block_scan(c0 + c1, warp_sums, total);
+    if (before < need && before + c0 + c1 >= need) {
+      const int digit = before + c0 >= need ? d0 : d1;
+      const int above = before + c0 >= need ? before : before + c0;
+      sel_prefix = prefix | ((uint32_t)digit << shift);
+      sel_mask = mask | (dmask << shift);
+      sel_remaining = need - above;
     }
+    if (tid == 0 && total < need) sel_remaining = -1;  // fewer than K candidates (first pass only)
     __syncthreads();
     if (sel_remaining < 0) break;
   }
