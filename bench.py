@@ -1,17 +1,31 @@
 """Benchmark of the sparse paged GQA FP8 decode path (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config 1] [--kernel auto|tc|simt] [--op decode|cache_write|topk]
+                    [--config 1|2|3|4] [--kernel auto|tc|simt] [--op decode|cache_write|topk]
 
-Workload: BASELINE's headline shape, configs[1] (256 requests x 32q/8kv heads x
-d128, page 16, 32 pages/request, Top-K 512 = every token in random order) on
-every GPU -- one process per GPU under torchrun, requests sharded by rank
-with no data-path collective, so per-GPU work is fixed ("weak" scaling; at 8
-GPUs the job is configs[3]'s 2048 requests). A step is one decode call over
-the rank's batch with all inputs resident in HBM; L2 is flushed between timed
-steps, outside the timed events: a 256 MiB write, then a 256 MiB read, so
-that the write's dirty lines go back to HBM before the next step instead of
-during it (``us_per_call_write_flush`` reports the write-only flush).
+Workload (``--config``), one process per GPU under torchrun, requests sharded
+by rank with no data-path collective:
+
+* 1 (default) -- BASELINE's headline shape, configs[1] (256 requests x 32q/8kv
+  heads x d128, page 16, 32 pages/request, Top-K 512 = every token in random
+  order) on every GPU: per-GPU work is fixed ("weak" scaling; at 8 GPUs the
+  job is 2048 requests);
+* 3 -- configs[3]: 2048 requests of the configs[1] shape split into N
+  contiguous ranges (``shard.contiguous_shards``), "strong" scaling;
+* 4 -- configs[4]: 1024 ragged requests (Hq 64, context 32768, Top-K lengths
+  U[64, 2048]) in N longest-processing-time bins (``shard.lpt_bins``),
+  "strong" scaling;
+* 2 -- configs[2] (context 8192, Top-K 512 sampled) on every GPU, weak.
+
+Each rank generates only its own requests and their pages on its GPU. A step
+is one decode call over the rank's batch with all inputs resident in HBM; L2
+is flushed between timed steps, outside the timed events: a 256 MiB write,
+then a 256 MiB read, so that the write's dirty lines go back to HBM before
+the next step instead of during it (``us_per_call_write_flush`` reports the
+write-only flush). After the timed steps each rank checks a sample of its
+rows against an fp32 torch restatement of the reference's eager path run on
+its GPU (``parity``), and the line lists every rank's time, clock and check
+(``per_rank``).
 
 Reported ``value``: achieved HBM TB/s on unique FP8 K/V bytes summed over
 ranks / max-over-ranks device time per call (the north star's figure);
@@ -19,13 +33,17 @@ ranks / max-over-ranks device time per call (the north star's figure);
 figure through the public ``qsa_decode`` call with the step's inputs (Q,
 gate, Top-K indices, block table, request map) copied from pinned host memory
 and the output copied back inside the timed region, as a serving loop runs
-it: three streams, so that step i's copies overlap the decode of step i-1;
-the K/V cache stays resident (it is the cache). ``--impl reference`` times the reference's eager
-path (a port of sm89_torch.torch_eager) on the host CPU instead.
+it: three streams, so that step i's copies overlap the decode of step i-1,
+with each stage timed on its own stream (``e2e.stages``); the K/V cache stays
+resident (it is the cache). At N=1 with the default workload, ``per_config``
+adds configs[2] and configs[4] (whole batch on one GPU) timed the same way.
+``--impl reference`` times the reference's eager path (a port of
+sm89_torch.torch_eager) on the host CPU instead.
 
 ``--op cache_write`` (one GPU) times the paged cache writer instead: the
 whole configs[1] cache (256 requests x 512 tokens x 8 KV heads) written from
 bf16 keys and values at the block table's slots, GB/s of bytes moved.
+``--op topk`` times the Top-K index producer on configs[4]'s shape.
 """
 
 from __future__ import annotations
@@ -69,10 +87,15 @@ class L2Flush:
 
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch on
-# the bench workload, from the ncu capture summarised in profiles/ (None until
-# captured for the current kernel).
-NCU_TRAFFIC_BYTES = {("configs[1]", "tc"): 278_676_480, ("cache write", 1): 772_670_000}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch on the bench
+# workload, from an ncu capture (not measured by this run): (bytes, which
+# capture). None where no capture of the kernel exists.
+NCU_TRAFFIC = {
+    ("configs[1]", "tc"): (278_676_480, "ncu --set full capture of one qsa_decode_tc_kernel<4,0> launch at "
+                                        "configs[1], clean caches; not measured by this run"),
+    ("cache write", 1): (772_670_000, "ncu capture of one qsa_cache_write_kernel launch on the configs[1] "
+                                      "cache; not measured by this run"),
+}
 
 
 def parse():
@@ -85,6 +108,8 @@ def parse():
     ap.add_argument("--kernel", default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", choices=["decode", "cache_write", "topk"], default="decode")
+    ap.add_argument("--no-per-config", action="store_true", help="skip the configs[2]/[4] block at N=1")
+    ap.add_argument("--check-rows", type=int, default=8, help="rows per rank checked after the timed steps")
     return ap.parse_args()
 
 
@@ -152,7 +177,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
     }
 
-    def __init__(self, index: int, period_s: float = 0.005):
+    def __init__(self, index: int, period_s: float = 0.001):
         self.samples, self.reasons, self.ok = [], set(), False
         self.period = period_s
         self._stop = threading.Event()
@@ -239,6 +264,17 @@ def reduce_max(x: float, world: int, local: int) -> float:
     return float(t.item())
 
 
+def gather_objects(obj, world: int):
+    """Every rank's ``obj`` in rank order (control plane only)."""
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
 def reduce_sum(x: float, world: int, local: int) -> float:
     if world == 1:
         return x
@@ -248,6 +284,100 @@ def reduce_sum(x: float, world: int, local: int) -> float:
     t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
+
+
+# --------------------------------------------------------------- workloads --
+SCALING = {0: "weak", 1: "weak", 2: "weak", 3: "strong", 4: "strong"}
+
+
+def rank_rows(cfg: int, rank: int, world: int):
+    """Which requests of the configuration rank ``rank`` of ``world`` holds:
+    ``(rows, row_ids, plan)`` -- a row count (weak scaling: the whole
+    configuration per rank) or the row ids of its shard (configs[3]:
+    contiguous ranges of the 2048 requests; configs[4]: longest-processing-
+    time bins over the 1024 ragged Top-K lengths)."""
+    from qsa_b200.inputs import CONFIGS, ragged_lengths
+    from qsa_b200.shard import bin_loads, contiguous_shards, lpt_bins
+
+    total = CONFIGS[cfg]["rows"]
+    if cfg == 3:
+        lo, hi = contiguous_shards(total, world)[rank]
+        return None, list(range(lo, hi)), f"contiguous rows [{lo}, {hi}) of {total}"
+    if cfg == 4:
+        lengths = ragged_lengths(CONFIGS[4], total, seed=0)
+        bins = lpt_bins(lengths, world)
+        loads = bin_loads(lengths, bins)
+        return None, bins[rank], (f"LPT bin {rank} of {world}: {len(bins[rank])} of {total} rows, "
+                                  f"{loads[rank]} of {sum(loads)} Top-K entries (bins {min(loads)}-{max(loads)})")
+    return total, None, f"all {total} rows of the configuration on every rank"
+
+
+def make_rank_workload(cfg: int, dev, rank: int, world: int):
+    from qsa_b200.inputs import make_workload
+
+    rows, row_ids, plan = rank_rows(cfg, rank, world)
+    w = make_workload(cfg, dev, seed=0, rows=rows, row_ids=row_ids, shard=rank)
+    return w, plan
+
+
+def bench_config(cfg: int, world: int, rows_per_gpu: int, rows_total: int) -> dict:
+    """The ``config`` object, identical in both arms for one --config / N."""
+    from qsa_b200.inputs import CONFIGS
+
+    c = CONFIGS[cfg]
+    return {"workload": workload_name(cfg), "rows_per_gpu": rows_per_gpu, "rows_total": rows_total,
+            "hq": c["hq"], "hkv": c["hkv"], "head_dim": 128, "page": c["page"], "pages_per_req": c["ppr"],
+            "topk": c["topk"], "parallelism": f"request-sharded x{world}, no collective"}
+
+
+def config_rows(cfg: int, world: int):
+    """(rows per GPU, rows in the job): the largest shard for strong scaling."""
+    from qsa_b200.inputs import CONFIGS
+
+    total = CONFIGS[cfg]["rows"]
+    if SCALING[cfg] == "weak":
+        return total, total * world
+    return max(len(rank_rows(cfg, r, world)[1]) for r in range(world)), total
+
+
+def torch_check(w, out, n_rows: int):
+    """Parity sample of the bench: ``n_rows`` rows of the rank's output
+    against an fp32 restatement, in torch ops on the GPU, of the reference's
+    eager path (sm89_torch.py:30-54: index decode, block-table gather, fp32
+    QK, masked softmax, PV, sigmoid gate), with the count rule and zeros for
+    an empty row. Returns (max abs error, all within atol/rtol 2e-2)."""
+    import torch
+
+    dev = out.device
+    rows = torch.linspace(0, w.rows - 1, steps=min(n_rows, w.rows), device=dev).round().long().unique()
+    page, hkv = w.meta["page"], w.meta["hkv"]
+    hq = w.q.shape[1]
+    grp = hq // hkv
+    ppr = w.btable.shape[1]
+    num_pages = w.k.shape[0]
+    idx = w.indices[rows].long()
+    valid = (idx >= 0) & (idx // page < ppr)
+    if w.counts is not None:
+        valid &= torch.arange(idx.shape[1], device=dev)[None, :] < w.counts[rows].long()[:, None]
+    req = w.t2r[rows].long()
+    valid &= (req >= 0)[:, None] & (req < w.btable.shape[0])[:, None]
+    lp = (idx.clamp(min=0) // page).clamp(max=ppr - 1)
+    phys = w.btable[req.clamp(0, w.btable.shape[0] - 1)[:, None], lp].long()
+    valid &= (phys >= 0) & (phys < num_pages)
+    slot = phys.clamp(0, num_pages - 1) * page + idx.clamp(min=0) % page
+    rows8 = lambda c: c.view(torch.uint8).view(num_pages * page, hkv, 128)
+    kf = rows8(w.k)[slot].view(torch.float8_e4m3fn).float()  # [n, K, hkv, 128]
+    vf = rows8(w.v)[slot].view(torch.float8_e4m3fn).float()
+    q = w.q[rows].float().view(-1, hkv, grp, 128)
+    sc = torch.einsum("nghd,nkgd->nghk", q, kf) * (w.k_scale * w.softmax_scale)
+    sc = sc.masked_fill(~valid[:, None, None, :], float("-inf"))
+    pr = torch.nan_to_num(torch.softmax(sc, dim=-1), nan=0.0)
+    ctx = torch.einsum("nghk,nkgd->nghd", pr, vf) * w.v_scale
+    ref = (ctx * torch.sigmoid(w.gate[rows].float().view(-1, hkv, grp, 128))).view(-1, hq, 128)
+    got = out[rows].float()
+    err = (got - ref).abs()
+    ok = bool((err <= 2e-2 + 2e-2 * ref.abs()).all())
+    return float(err.max()), ok, int(rows.numel())
 
 
 # ------------------------------------------------------------ CPU baseline --
@@ -287,7 +417,9 @@ def cpu_eager_sample(w, rows: int, calls: int, warmup: int):
 
 
 def run_reference_arm(args):
-    """--impl reference: the reference's eager path on the host CPU."""
+    """--impl reference: the reference's eager path on the host CPU, on a
+    bounded sample of rank 0's requests (each step one eager call), with the
+    same ``config`` as this arm's line for the same --config and N."""
     import torch
 
     rank = int(os.environ.get("RANK", "0"))
@@ -295,25 +427,38 @@ def run_reference_arm(args):
         return 0
     from qsa_b200.inputs import make_workload
 
-    w = make_workload(args.config, "cpu", seed=0)
+    cfg = args.config
+    rows_gpu, rows_total = config_rows(cfg, args.gpus)
+    _, row_ids, _ = rank_rows(cfg, 0, args.gpus)
+
+    def sample_workload(n):
+        if row_ids is not None:
+            return make_workload(cfg, "cpu", seed=0, row_ids=row_ids[:n])
+        return make_workload(cfg, "cpu", seed=0, rows=n)
+
     # one step = one eager call on a bounded sample of the batch, sized so the
     # whole --steps/--warmup run stays within a few minutes
-    probe, _, _ = cpu_eager_sample(w, 8, 1, 1)
-    per_row = max(probe[0] / 8, 1e-4)
+    # (configs[4] generates each sampled request's whole 32768-token context
+    # on the host, 64 MiB of K+V a request, so its sample stays small)
+    cap = 8 if cfg == 4 else rows_gpu
+    probe_w = sample_workload(min(2 if cfg == 4 else 8, rows_gpu))
+    probe, _, _ = cpu_eager_sample(probe_w, probe_w.rows, 1, 1)
+    per_row = max(probe[0] / probe_w.rows, 1e-4)
     budget = 120.0 / max(1, args.steps + args.warmup)
-    rows = int(max(4, min(w.rows, budget / per_row)))
+    rows = int(max(min(2, rows_gpu), min(cap, budget / per_row)))
+    del probe_w
+    w = sample_workload(rows)
     times, unique_kv, threads = cpu_eager_sample(w, rows, args.steps, args.warmup)
     med = statistics.median(times)
     value = unique_kv / med / 1e12
-    sample = (f"{rows} of {w.rows} requests of {workload_name(args.config)} per call (unique K/V "
-              f"{unique_kv} B), {args.steps} timed calls after {args.warmup} warm-up, median")
+    sample = (f"{rows} of the {rows_gpu} requests of one GPU's share of {workload_name(cfg)} per call (unique "
+              f"K/V {unique_kv} B), {args.steps} timed calls after {args.warmup} warm-up, median")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3,
-        "us_per_call_full_batch": med / rows * w.rows * 1e6, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload_name(args.config), "rows": rows, "topk": w.meta["topk"],
-                   "hq": w.meta["hq"], "hkv": w.meta["hkv"], "head_dim": 128, "page": w.meta["page"]},
+        "us_per_call_full_batch": med / rows * rows_gpu * 1e6, "higher_is_better": True,
+        "scaling": SCALING[cfg], "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": bench_config(cfg, args.gpus, rows_gpu, rows_total),
         "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port", "sample": sample,
                          "min_s": min(times), "median_s": med, "max_s": max(times)},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -323,6 +468,197 @@ def run_reference_arm(args):
 
 
 # ---------------------------------------------------------------- our arm ---
+def decode_launches(w, kernel, dev) -> int:
+    """Kernels one decode call launches: tensor-core path, the row-map kernel
+    and the decode kernel (+ the split combine for Top-K rows longer than one
+    chunk, unless the decode merges the chunks itself); CUDA-core path, the
+    decode kernel (+ combine)."""
+    import torch
+
+    from qsa_b200 import ops
+
+    hq, hkv, topk = w.meta["hq"], w.meta["hkv"], w.meta["topk"]
+    tc_path = kernel == "tc" or (kernel == "auto" and ops.tc_supports_group(hq // hkv))
+    merged = tc_path and ops.tc_merges_chunks(w.rows, hq, hkv, topk,
+                                              torch.cuda.get_device_properties(dev).multi_processor_count)
+    return (2 if tc_path else 1) + (1 if topk > ops.chunk_tokens(hq, hkv) and not merged else 0)
+
+
+def time_steps(call, flush, stream, steps: int, warmup: int, write_only: bool = False):
+    """CUDA-event time (ms) of each of ``steps`` calls on ``stream``, L2
+    flushed between them outside the events."""
+    import torch
+
+    for _ in range(max(3, warmup)):
+        call()
+        flush(write_only)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for i in range(steps):
+        starts[i].record(stream)
+        call()
+        ends[i].record(stream)
+        flush(write_only)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+class E2EPipeline:
+    """The serving loop of the end-to-end figure on three streams: the
+    host->device copy of step i's inputs (from pinned memory), the decode of
+    step i and the device->host copy of its output each wait for their own
+    step's previous stage, so that step i's copies overlap the decode of step
+    i-1. Inputs and outputs are double-buffered on the device. ``run(steps)``
+    enqueues the steps directly; ``capture(steps)`` records the same steps
+    into one CUDA graph (what a serving loop replays so that the host's
+    per-call launch work leaves the critical path)."""
+
+    NAMES = ("q", "gate", "indices", "btable", "t2r")
+    NBUF = 2
+
+    def __init__(self, w, kernel, dev):
+        import torch
+
+        self.w, self.kernel, self.dev = w, kernel, dev
+        self.host_in = {k: getattr(w, k).cpu().pin_memory() for k in self.NAMES}
+        self.dev_in = [{k: torch.empty_like(getattr(w, k)) for k in self.NAMES} for _ in range(self.NBUF)]
+        self.dev_out = [torch.empty_like(w.q) for _ in range(self.NBUF)]
+        self.host_out = [torch.empty(w.q.shape, dtype=w.q.dtype, pin_memory=True) for _ in range(self.NBUF)]
+        self.h2d = sum(t.numel() * t.element_size() for t in self.host_in.values())
+        self.d2h = self.host_out[0].numel() * self.host_out[0].element_size()
+        self.s_in, self.s_dec, self.s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        self.ev_in = [torch.cuda.Event() for _ in range(self.NBUF)]
+        self.ev_dec = [torch.cuda.Event() for _ in range(self.NBUF)]
+        self.ev_out = [torch.cuda.Event() for _ in range(self.NBUF)]
+        self.stage_events = None
+
+    def step(self, i, stages=None, first=False):
+        """Step i; ``first``: no earlier step used its buffers (inside a
+        capture, the waits on the previous replay's events are left out; the
+        replays themselves are ordered on their launch stream)."""
+        import torch
+
+        import qsa_b200
+
+        b = i % self.NBUF
+        w = self.w
+        rec = (lambda k: stages[k][i].record()) if stages is not None else (lambda k: None)
+        with torch.cuda.stream(self.s_in):
+            if not first:
+                self.s_in.wait_event(self.ev_dec[b])  # the decode of step i - NBUF has read dev_in[b]
+            rec(0)
+            for k in self.NAMES:
+                self.dev_in[b][k].copy_(self.host_in[k], non_blocking=True)
+            rec(1)
+            self.ev_in[b].record(self.s_in)
+        with torch.cuda.stream(self.s_dec):
+            self.s_dec.wait_event(self.ev_in[b])
+            if not first:
+                self.s_dec.wait_event(self.ev_out[b])  # dev_out[b] of step i - NBUF has been copied out
+            rec(2)
+            d = self.dev_in[b]
+            qsa_b200.qsa_decode(d["q"], w.k, w.v, w.k_scale, w.v_scale, d["btable"], d["t2r"], d["indices"],
+                                d["gate"], out=self.dev_out[b], kernel=self.kernel)
+            rec(3)
+            self.ev_dec[b].record(self.s_dec)
+        with torch.cuda.stream(self.s_out):
+            self.s_out.wait_event(self.ev_dec[b])
+            rec(4)
+            self.host_out[b].copy_(self.dev_out[b], non_blocking=True)
+            rec(5)
+            self.ev_out[b].record(self.s_out)
+
+    def run(self, steps, timed_stages=False):
+        """Enqueues ``steps`` steps; returns (device ms per step, host ms per
+        step, per-stage mean ms [h2d, decode, d2h] or None)."""
+        import torch
+
+        stages = None
+        if timed_stages:
+            stages = [[torch.cuda.Event(enable_timing=True) for _ in range(steps)] for _ in range(6)]
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.s_in)
+        t0 = time.perf_counter()
+        for i in range(steps):
+            self.step(i, stages)
+        host_ms = (time.perf_counter() - t0) * 1e3 / steps
+        e1.record(self.s_out)  # after the last step's device->host copy
+        torch.cuda.synchronize()
+        means = None
+        if stages is not None:
+            means = [statistics.fmean(stages[2 * j][i].elapsed_time(stages[2 * j + 1][i]) for i in range(steps))
+                     for j in range(3)]
+        return e0.elapsed_time(e1) / steps, host_ms, means
+
+    def capture(self, steps):
+        import torch
+
+        g = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(self.dev)
+        with torch.cuda.graph(g, stream=cap):
+            fork = torch.cuda.Event()
+            fork.record(cap)
+            for s in (self.s_in, self.s_dec, self.s_out):
+                s.wait_event(fork)
+            for i in range(steps):
+                self.step(i, first=i < self.NBUF)
+            for s in (self.s_in, self.s_dec, self.s_out):
+                join = torch.cuda.Event()
+                join.record(s)
+                cap.wait_event(join)
+        return g, cap
+
+    def replay(self, g, cap, steps):
+        """Device ms per step of one replay of a ``steps``-step graph."""
+        import torch
+
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(cap):
+            e0.record(cap)
+            g.replay()
+            e1.record(cap)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    def last_output(self, steps):
+        b = (steps - 1) % self.NBUF
+        return self.host_out[b], self.dev_out[b]
+
+
+def per_config_block(dev, kernel, steps, warmup, flush, peak, peak_kind):
+    """configs[2] and configs[4] (the whole batch on this one GPU), timed like
+    the headline: L2 flushed between calls, CUDA events, mean over ``steps``."""
+    import torch
+
+    import qsa_b200
+    from qsa_b200.inputs import kv_bytes, make_workload
+
+    block = {}
+    stream = torch.cuda.current_stream()
+    for cfg in (2, 4):
+        w = make_workload(cfg, dev, seed=0)
+        acct = kv_bytes(w)
+        out = torch.empty_like(w.q)
+        call = lambda: qsa_b200.qsa_decode(*w.args(), out=out, kernel=kernel)
+        ms = statistics.fmean(time_steps(call, flush, stream, steps, warmup))
+        err, ok, n = torch_check(w, out, 8)
+        gbs = acct["algorithmic"] / (ms * 1e-3) / 1e9
+        block[workload_name(cfg)] = {
+            "rows": w.rows, "us_per_call": ms * 1e3, "unique_kv_tbs": acct["unique_kv"] / (ms * 1e-3) / 1e12,
+            "logical_kv_tbs": acct["logical_kv"] / (ms * 1e-3) / 1e12, "achieved_gbs": gbs,
+            "frac": gbs / peak, "frac_unique_kv": acct["unique_kv"] / (ms * 1e-3) / 1e9 / peak,
+            "peak_source": peak_kind, "bytes": {k: acct[k] for k in ("unique_kv", "logical_kv", "algorithmic")},
+            "launches_per_call": decode_launches(w, kernel, dev),
+            "parity": {"rows_checked": n, "max_abs_err": err, "ok": ok},
+        }
+        del w, out
+        torch.cuda.empty_cache()
+    return block
+
+
 def run_ours(args):
     import torch
 
@@ -331,23 +667,18 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     all_cpus = os.sched_getaffinity(0)
     numa_bound = bind_local_cpus(local)
-    import qsa_b200
-    from qsa_b200 import capi, ops
-    from qsa_b200.inputs import kv_bytes, make_workload
+    from qsa_b200 import capi
+    from qsa_b200.inputs import kv_bytes
 
-    w = make_workload(args.config, dev, seed=0, shard=rank)
+    import qsa_b200
+
+    cfg = args.config
+    w, plan = make_rank_workload(cfg, dev, rank, world)
     acct = kv_bytes(w)
     flush = L2Flush(dev)
     out = torch.empty_like(w.q)
     kernel = args.kernel
-    # tensor-core path: the row-map kernel and the decode kernel (+ the split
-    # combine for Top-K rows longer than one chunk, unless the decode merges
-    # the chunks itself); CUDA-core path: the decode kernel (+ combine)
-    chunk = ops.chunk_tokens(w.meta["hq"], w.meta["hkv"])
-    tc_path = kernel == "tc" or (kernel == "auto" and ops.tc_supports_group(w.meta["hq"] // w.meta["hkv"]))
-    merged = tc_path and ops.tc_merges_chunks(w.rows, w.meta["hq"], w.meta["hkv"], w.meta["topk"],
-                                              torch.cuda.get_device_properties(dev).multi_processor_count)
-    launches_per_call = (2 if tc_path else 1) + (1 if w.meta["topk"] > chunk and not merged else 0)
+    launches_per_call = decode_launches(w, kernel, dev)
 
     def call():
         qsa_b200.qsa_decode(*w.args(), out=out, kernel=kernel)
@@ -361,136 +692,133 @@ def run_ours(args):
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier(world, local)
     with ClockSampler(local) as clk:
-        region0 = torch.cuda.Event(enable_timing=True)
-        region1 = torch.cuda.Event(enable_timing=True)
-        region0.record(stream)
         for i in range(args.steps):
             starts[i].record(stream)
             call()
             ends[i].record(stream)
             flush()
-        region1.record(stream)
         barrier(world, local)
     kern_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    local_ms = statistics.fmean(kern_ms)
+    # parity sample of the timed output (every timed call wrote the same out)
+    chk_err, chk_ok, chk_n = torch_check(w, out, args.check_rows)
     # the same steps after a write-only flush, for comparison: the flush's
     # dirty lines then go back to HBM during the step
-    for i in range(args.steps):
-        starts[i].record(stream)
-        call()
-        ends[i].record(stream)
-        flush(write_only=True)
+    wf_local = statistics.fmean(time_steps(call, flush, stream, args.steps, 0, write_only=True))
     barrier(world, local)
-    wf_ms = reduce_max(sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps, world, local)
-    local_ms = sum(kern_ms) / len(kern_ms)
+    wf_ms = reduce_max(wf_local, world, local)
     step_ms = reduce_max(local_ms, world, local)
     total_unique = reduce_sum(acct["unique_kv"], world, local)
     total_logical = reduce_sum(acct["logical_kv"], world, local)
     value = total_unique / (step_ms * 1e-3) / 1e12
 
     # ---- end to end through the public call with host buffers ---------------
-    # A serving loop's pipeline on three streams: the host->device copy of
-    # step i's inputs (from pinned memory), the decode of step i and the
-    # device->host copy of its output each wait for their own step's previous
-    # stage, so step i's copies overlap the decode of step i-1. Inputs and
-    # outputs are double-buffered on the device. The timed region spans all
-    # steps, every copy included; the resident K/V (larger than L2) is read
-    # from HBM by every decode, so no flush is needed between steps.
-    names = ("q", "gate", "indices", "btable", "t2r")
-    host_in = {k: getattr(w, k).cpu().pin_memory() for k in names}
-    nbuf = 2
-    dev_in = [{k: torch.empty_like(getattr(w, k)) for k in names} for _ in range(nbuf)]
-    dev_out = [torch.empty_like(w.q) for _ in range(nbuf)]
-    host_out = [torch.empty(w.q.shape, dtype=w.q.dtype, pin_memory=True) for _ in range(nbuf)]
-    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
-    d2h = host_out[0].numel() * host_out[0].element_size()
-    s_in, s_dec, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(nbuf)]
-    ev_dec = [torch.cuda.Event() for _ in range(nbuf)]
-    ev_out = [torch.cuda.Event() for _ in range(nbuf)]
-
-    def e2e_step(i):
-        b = i % nbuf
-        with torch.cuda.stream(s_in):
-            s_in.wait_event(ev_dec[b])  # the decode of step i - nbuf has read dev_in[b]
-            for k in names:
-                dev_in[b][k].copy_(host_in[k], non_blocking=True)
-            ev_in[b].record(s_in)
-        with torch.cuda.stream(s_dec):
-            s_dec.wait_event(ev_in[b])
-            s_dec.wait_event(ev_out[b])  # dev_out[b] of step i - nbuf has been copied out
-            d = dev_in[b]
-            qsa_b200.qsa_decode(d["q"], w.k, w.v, w.k_scale, w.v_scale, d["btable"], d["t2r"], d["indices"],
-                                d["gate"], out=dev_out[b], kernel=kernel)
-            ev_dec[b].record(s_dec)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev_dec[b])
-            host_out[b].copy_(dev_out[b], non_blocking=True)
-            ev_out[b].record(s_out)
-
-    for i in range(max(3, args.warmup)):
-        e2e_step(i)
-    torch.cuda.synchronize()
+    pipe = E2EPipeline(w, kernel, dev)
+    pipe.run(max(3, args.warmup))
     barrier(world, local)
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(s_in)
-    for i in range(args.steps):
-        e2e_step(i)
-    e_end.record(s_out)  # after the last step's device->host copy
-    torch.cuda.synchronize()
+    eager_ms, host_ms, stage_ms = pipe.run(args.steps, timed_stages=True)
     barrier(world, local)
-    e2e_ms = reduce_max(e_start.elapsed_time(e_end) / args.steps, world, local)
+    eager_ms_max = reduce_max(eager_ms, world, local)
+    h_out, d_out = pipe.last_output(args.steps)
+    assert torch.equal(h_out, d_out.cpu()) and torch.equal(d_out, out)
+    g, cap = pipe.capture(args.steps)
+    pipe.replay(g, cap, args.steps)  # warm-up replay
+    barrier(world, local)
+    graph_ms = pipe.replay(g, cap, args.steps)
+    barrier(world, local)
+    graph_ms_max = reduce_max(graph_ms, world, local)
+    h_out, d_out = pipe.last_output(args.steps)
+    assert torch.equal(h_out, d_out.cpu()) and torch.equal(d_out, out)
+    del g
+    e2e_ms = graph_ms_max
     e2e_value = total_unique / (e2e_ms * 1e-3) / 1e12
-    last = (args.steps - 1) % nbuf
-    assert torch.equal(host_out[last], dev_out[last].cpu())
-    assert torch.equal(dev_out[last], out)  # the pipelined decode reproduces the device-resident one
+    h2d_us, dec_us, d2h_us = (x * 1e3 for x in stage_ms)
     dev_err = capi.device_error()
+
+    # ---- per-rank record ------------------------------------------------------
+    clocks = clk.summary()
+    mine = {"rank": rank, "rows": w.rows, "plan": plan, "us_per_call": local_ms * 1e3,
+            "sm_mhz": clocks["sm_mhz"], "clock_reasons": clocks["reasons"], "unique_kv": acct["unique_kv"],
+            "parity": {"rows_checked": chk_n, "max_abs_err": chk_err, "ok": chk_ok},
+            "e2e_us_per_step": graph_ms * 1e3, "e2e_eager_us_per_step": eager_ms * 1e3,
+            "device_error": dev_err}
+    ranks = gather_objects(mine, world)
+    slowest = max(ranks, key=lambda r: r["us_per_call"])
 
     # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         os.sched_setaffinity(0, all_cpus)  # the CPU baseline gets every core again
-        times, ukv, threads = cpu_eager_sample(w, 32, 5, 3)
+        n_cpu = min(8 if cfg == 4 else 32, w.rows)
+        times, ukv, threads = cpu_eager_sample(w, n_cpu, 5, 3)
         med = statistics.median(times)
         cpu = {"value": ukv / med / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
-               "sample": f"32 of {w.rows} requests of {workload_name(args.config)} per call through the "
+               "sample": f"{n_cpu} of {w.rows} requests of {workload_name(cfg)} per call through the "
                          f"reference's eager ATen sequence on CPU (oracle/eager_port.py), median of 5 after 3 "
                          f"warm-up; min {min(times):.3f} s, max {max(times):.3f} s per call",
-               "us_per_call_full_batch": med / 32 * w.rows * 1e6}
+               "us_per_call_full_batch": med / n_cpu * w.rows * 1e6}
 
     peak, peak_kind = peaks()
+    per_config = None
+    if rank == 0 and world == 1 and cfg == 1 and not args.no_per_config:
+        del pipe
+        pc_steps = max(3, min(args.steps, 50))
+        per_config = per_config_block(dev, kernel, pc_steps, args.warmup, flush, peak, peak_kind)
+
     achieved_gbs = acct["algorithmic"] / (local_ms * 1e-3) / 1e9
     kname = "tc" if kernel in ("auto", "tc") else kernel
-    traffic = NCU_TRAFFIC_BYTES.get((workload_name(args.config), kname))
-    clocks = clk.summary()
+    traffic, traffic_source = NCU_TRAFFIC.get((workload_name(cfg), kname), (None, None))
+    rows_gpu, rows_total = config_rows(cfg, world)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "us_per_call": step_ms * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": SCALING[cfg], "vs_baseline": None,
             "dtype": "e4m3 tensor-core MMA, f32 accumulate/softmax, bf16 out", "data": "synthetic",
-            "config": {"workload": workload_name(args.config), "rows_per_gpu": w.rows, "rows_total": w.rows * world,
-                       "hq": w.meta["hq"], "hkv": w.meta["hkv"], "head_dim": 128, "page": w.meta["page"],
-                       "pages_per_req": w.meta["ppr"], "topk": w.meta["topk"], "kernel": kernel,
-                       "l2": L2_NOTE,
-                       "parallelism": f"request-sharded x{world}, no collective"},
+            "config": bench_config(cfg, world, rows_gpu, rows_total),
+            "kernel": kernel, "l2": L2_NOTE,
             "us_per_call_write_flush": wf_ms * 1e3,
             "bytes_per_gpu": {"unique_kv": acct["unique_kv"], "logical_kv": acct["logical_kv"],
                               "algorithmic": acct["algorithmic"]},
             "logical_kv_tbs": total_logical / (step_ms * 1e-3) / 1e12,
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                          "frac": achieved_gbs / peak, "peak_source": peak_kind,
-                         "traffic": traffic, "kernel": f"qsa_decode_{kname}_kernel",
-                         "timed": "whole call (row-map kernel + decode kernel), CUDA events on the launch stream"},
+                         "frac_unique_kv": acct["unique_kv"] / (local_ms * 1e-3) / 1e9 / peak,
+                         "traffic": traffic, "traffic_source": traffic_source,
+                         "kernel": f"qsa_decode_{kname}_kernel",
+                         "timed": "whole call (row-map kernel + decode kernel), CUDA events on the launch stream, "
+                                  "rank 0"},
+            "parity": {"ok": all(r["parity"]["ok"] for r in ranks),
+                       "max_abs_err": max(r["parity"]["max_abs_err"] for r in ranks),
+                       "rows_checked": sum(r["parity"]["rows_checked"] for r in ranks),
+                       "against": "fp32 torch restatement of the reference's eager path on each rank's GPU, "
+                                  "atol 2e-2 / rtol 2e-2"},
+            "per_rank": ranks,
+            "slowest_rank": {"rank": slowest["rank"], "us_per_call": slowest["us_per_call"],
+                             "sm_mhz": slowest["sm_mhz"], "rows": slowest["rows"],
+                             "unique_kv": slowest["unique_kv"]},
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms,
-                    "method": "3-stream pipeline: step i's host->device inputs and device->host output overlap "
-                              "the decode of step i-1; all steps' copies inside the timed region",
+            "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": pipe_h2d(w),
+                    "d2h_bytes_per_step": pipe_d2h(w), "ms_per_step": e2e_ms,
+                    "method": "3-stream serving pipeline (step i's host->device inputs and device->host output "
+                              "overlap the decode of step i-1) captured as one CUDA graph of all timed steps and "
+                              "replayed; every step's copies inside the timed region",
+                    "eager": {"value": total_unique / (eager_ms_max * 1e-3) / 1e12, "ms_per_step": eager_ms_max,
+                              "host_enqueue_ms_per_step": host_ms,
+                              "method": "the same steps enqueued call by call from Python"},
+                    "stages_us": {"h2d": h2d_us, "decode": dec_us, "d2h": d2h_us,
+                                  "h2d_gbs": pipe_h2d(w) / (h2d_us * 1e-6) / 1e9,
+                                  "d2h_gbs": pipe_d2h(w) / (d2h_us * 1e-6) / 1e9,
+                                  "slowest": max(("h2d", h2d_us), ("decode", dec_us), ("d2h", d2h_us),
+                                                 key=lambda x: x[1])[0],
+                                  "note": "mean per-step stage times on their own streams, eager run, rank 0"},
                     "host_cpus_bound_to_gpu_numa_node": numa_bound},
             "gpu_launches": launches_per_call * args.steps,
             "clocks": clocks,
-            "device_error": dev_err,
+            "device_error": max(r["device_error"] for r in ranks),
         }
+        if per_config is not None:
+            line["per_config"] = per_config
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -498,6 +826,14 @@ def run_ours(args):
         barrier(world, local)
         dist.destroy_process_group()
     return 0
+
+
+def pipe_h2d(w) -> int:
+    return sum(getattr(w, k).numel() * getattr(w, k).element_size() for k in E2EPipeline.NAMES)
+
+
+def pipe_d2h(w) -> int:
+    return w.q.numel() * w.q.element_size()
 
 
 # ------------------------------------------------------------ cache writer --
@@ -606,7 +942,7 @@ def run_cache_write(args):
         "config": {"workload": f"cache write of {workload_name(args.config)}", "tokens": tokens, "hkv": hkv,
                    "page": page, "l2": L2_NOTE},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                     "peak_source": peak_kind, "traffic": NCU_TRAFFIC_BYTES.get(("cache write", args.config)),
+                     "peak_source": peak_kind, "traffic": NCU_TRAFFIC.get(("cache write", args.config), (None,))[0],
                      "kernel": "qsa_cache_write_kernel",
                      "bytes_per_step": moved},
         "gpu_launches": args.steps,

@@ -54,7 +54,7 @@ enum {
   QSA_B200_OK = 0,
   QSA_B200_ERR_NULL_POINTER = -1, /* a required pointer is NULL */
   QSA_B200_ERR_BAD_SHAPE = -2,    /* a size is negative / inconsistent */
-  QSA_B200_ERR_UNSUPPORTED = -3,  /* head_dim != 128, or group > 32 */
+  QSA_B200_ERR_UNSUPPORTED = -3,  /* head_dim != 128, group > 32, or past a tensor-core kernel limit */
   QSA_B200_ERR_MISALIGNED = -4,   /* a tensor is not 16-byte aligned */
   QSA_B200_ERR_WORKSPACE = -5,    /* workspace missing or too small */
   QSA_B200_ERR_DEVICE = -6,       /* current device is not sm_100 */
@@ -66,7 +66,10 @@ enum {
 
 /* Kernel selection. AUTO picks the tensor-core kernel for group sizes
  * (Hq / Hkv) 1 to 8 and 10, 12, 14, 16, and the CUDA-core kernel for the
- * others (up to 32). */
+ * others (up to 32). The tensor-core kernel (explicit or through AUTO)
+ * returns QSA_B200_ERR_UNSUPPORTED for a cache of more than 2^31 - 1 rows of
+ * 128 bytes (num_pages * page_size * num_kv_heads; 256 GiB per cache) and
+ * for more than 2^30 - 1 work items (rows * num_kv_heads * ceil(topk / 512)). */
 enum { QSA_B200_KERNEL_AUTO = 0, QSA_B200_KERNEL_TC = 1, QSA_B200_KERNEL_SIMT = 2 };
 
 typedef struct qsa_b200_decode_args {

@@ -6,11 +6,12 @@
 #
 # TEST INFRASTRUCTURE ONLY: the GPU comparator tests load it to check the
 # build against the reference's fastest kernel on the same B200. It is built
-# from the reference checkout where it lies ($QSA_REFERENCE_DIR, or the
-# default location below); no reference source is copied into this repository.
+# from the reference checkout where it lies ($QSA_REFERENCE_DIR, else a
+# directory named "reference" beside this repository's own directory); no
+# reference source is copied into this repository.
 set -euo pipefail
 here="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-ref="${QSA_REFERENCE_DIR:-/root/reference}"
+ref="${QSA_REFERENCE_DIR:-$(dirname "$(dirname "$here")")/reference}"
 src="$ref/sm89_cuda.cu"
 if [[ ! -f "$src" ]]; then
   echo "reference source $src not found; oracle/_ref not rebuilt" >&2

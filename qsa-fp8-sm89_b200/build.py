@@ -59,7 +59,7 @@ def _stale(target: Path, deps) -> bool:
 def build_lib(force=False, verbose=False) -> Path:
     BUILD.mkdir(exist_ok=True)
     PKG.mkdir(exist_ok=True)
-    headers = [CSRC / h for h in HEADERS] + [INCLUDE / "qsa_b200.h"]
+    headers = [CSRC / h for h in HEADERS] + sorted(INCLUDE.glob("*.h"))
     objs = []
     for src in CU_SOURCES:
         obj = BUILD / (Path(src).stem + ".o")

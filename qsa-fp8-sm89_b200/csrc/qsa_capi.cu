@@ -14,12 +14,18 @@
 #include <cstdint>
 
 #include "../../include/qsa_b200.h"
+#include "../../include/qsa_b200_testing.h"
 #include "qsa_internal.h"
 
 namespace qsa {
 
 // Device error word (one per device that loads the library).
 __device__ int g_device_error = 0;
+
+constexpr uint64_t kDefaultWaitLimitNs = 1000000000ull;
+std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 namespace {
 
@@ -90,6 +96,16 @@ int check_decode_args(const qsa_b200_decode_args* a) {
   if (a->kernel == QSA_B200_KERNEL_TC && !tc_supports_group(group)) return QSA_B200_ERR_UNSUPPORTED;
   if (a->kernel < QSA_B200_KERNEL_AUTO || a->kernel > QSA_B200_KERNEL_SIMT) return QSA_B200_ERR_UNSUPPORTED;
   if ((int64_t)a->rows * a->num_kv_heads > 0x7fffffffll) return QSA_B200_ERR_BAD_SHAPE;
+  if (a->kernel == QSA_B200_KERNEL_TC || (a->kernel == QSA_B200_KERNEL_AUTO && tc_supports_group(group))) {
+    // the tensor-core kernel's limits: its row map holds token slots as
+    // int32 and its tensor maps address at most 2^31 - 1 (slot, KV head)
+    // rows of 128 bytes (256 GiB per cache); its work items are counted in
+    // int32
+    if (a->num_pages * a->page_size * a->num_kv_heads > 0x7fffffffll) return QSA_B200_ERR_UNSUPPORTED;
+    const int64_t chunk = tc_chunk_tokens(group);
+    const int64_t chunks = a->topk <= chunk ? 1 : (a->topk + chunk - 1) / chunk;
+    if ((int64_t)a->rows * a->num_kv_heads * chunks > 0x3fffffffll) return QSA_B200_ERR_UNSUPPORTED;
+  }
   if (a->rows == 0) return QSA_B200_OK;
   if (!a->q || !a->k_cache || !a->v_cache || !a->gate || !a->out) return QSA_B200_ERR_NULL_POINTER;
   if (!aligned16(a->q) || !aligned16(a->k_cache) || !aligned16(a->v_cache) || !aligned16(a->gate) ||
@@ -136,6 +152,7 @@ void fill_params(const qsa_b200_decode_args* a, DecodeParams* p) {
   p->item_counter = nullptr;
   p->merge_chunks = 0;
   p->err = nullptr;
+  p->wait_limit_ns = wait_limit_ns();
 }
 
 bool uses_tc(const qsa_b200_decode_args* a, int group) {
@@ -150,11 +167,14 @@ struct WorkspaceLayout {
   int64_t total() const { return rowmap_bytes + part_o_bytes + part_lse_bytes; }
 };
 
+// The split partials are left out when the tensor-core kernel merges the
+// chunks of each (row, KV head) itself (tc_merges_chunks on the current
+// device), since then nothing writes or reads them.
 WorkspaceLayout workspace_for(const DecodeParams& p, bool tc) {
   WorkspaceLayout w{0, 0, 0};
   if (tc)
     w.rowmap_bytes = align256((int64_t)p.rows * p.rowmap_stride * 4) + align256((int64_t)p.rows * p.num_chunks * 16) + 256;
-  if (p.num_chunks > 1) {
+  if (p.num_chunks > 1 && !(tc && tc_merges_chunks(p))) {
     const int64_t n = (int64_t)p.rows * p.num_q_heads * p.num_chunks;
     w.part_o_bytes = align256(n * 128 * 4);
     w.part_lse_bytes = align256(n * 4);
@@ -220,7 +240,7 @@ int qsa_b200_decode(const qsa_b200_decode_args* args, void* workspace, size_t wo
       p.item_counter = reinterpret_cast<int*>(reinterpret_cast<char*>(p.tile_flags) +
                                               align256((int64_t)p.rows * p.num_chunks * 16));
     }
-    if (p.num_chunks > 1) {
+    if (lay.part_o_bytes > 0) {
       p.part_o = reinterpret_cast<float*>(ws + lay.rowmap_bytes);
       p.part_lse = reinterpret_cast<float*>(ws + lay.rowmap_bytes + lay.part_o_bytes);
     }
@@ -354,6 +374,10 @@ int qsa_b200_topk_select(const qsa_b200_topk_args* a, qsa_b200_stream_t stream) 
 }
 
 int qsa_b200_last_status(void) { return t_last_status; }
+
+uint64_t qsa_b200_testing_set_wait_limit_ns(uint64_t ns) {
+  return g_wait_limit_ns.exchange(ns == 0 ? kDefaultWaitLimitNs : ns, std::memory_order_relaxed);
+}
 
 int qsa_b200_device_error(int clear) {
   int val = 0;

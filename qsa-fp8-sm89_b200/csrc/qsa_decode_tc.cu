@@ -54,10 +54,17 @@
 //
 // Every selected 128-byte K/V row is read from HBM once and shared by the G
 // query heads. Q and P keep their precision through a split into E4M3 terms:
-//   q * 2^E = t0 + t1/16                    (exact for bf16 q)
-//   p * 256 = t0 + t1/16 + t2/256 + t3/2048 (about 15 bits of p)
+//   q * 2^E = t0 + t1/16, where 2^E maps the head's largest |q| into
+//     [128, 256): exact for every bf16 element within 2^13 of that largest
+//     |q|; a smaller element keeps an absolute error of at most 2^-14 in the
+//     scaled domain (under 2^-21 of the largest |q|), and one below about
+//     2^-21 of it becomes 0 (E4M3's subnormals end at 2^-9);
+//   p * 256 = t0 + t1/16 + t2/256 + t3/2048: about 15 significant bits of p,
+//     and an absolute error under 2^-29 for the smallest p (p <= 1, the
+//     chunk's maximum being 1);
 // so the FP8 x FP8 tensor-core products reproduce the reference's fp32
-// products of the FP8 cache values with bf16 q and fp32 p.
+// products of the FP8 cache values with bf16 q and fp32 p to within those
+// bounds.
 //
 // Synchronisation is by mbarriers: kv_full/kv_empty per K/V ring slot,
 // meta_full/meta_empty per metadata slot, s_full/o_full/tmem_empty per TMEM
@@ -78,7 +85,7 @@ namespace {
 
 constexpr int kTile = 128;                    // tokens per tile
 constexpr int kTileBytes = kTile * kHeadDim;  // 16 KiB of FP8
-constexpr int kTermsQ = 2;                    // FP8 terms per query value (exact for bf16)
+constexpr int kTermsQ = 2;                    // FP8 terms per query value (bounds above)
 constexpr int kTermsP = 4;                    // FP8 terms per probability
 constexpr int kMeta = 4;                      // metadata ring depth (items)
 constexpr int kMaxTmemBufs = 3;               // TMEM accumulator buffers (items), at most
@@ -88,6 +95,8 @@ constexpr int kMmaWarp = 1 + kLoaders;
 constexpr int kSoftmax0 = kMmaWarp + 1;       // softmax / epilogue warps
 static_assert(kSoftmax0 % 4 == 0, "softmax warps must cover the four TMEM lane quadrants in order");
 constexpr int kSmemLimit = 232448;            // 227 KiB opt-in per CTA
+// Limit of the drain waits for a CTA's own copies and MMAs in flight (the
+// pipeline's waits take DecodeParams::wait_limit_ns, 1 s unless a test sets it).
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr int kErrTimeout = 1;
 
@@ -156,7 +165,7 @@ struct Cfg {
   static constexpr int kRedSum = align128(kRedMax + 2 * kSoftmaxWarps * GP * 4);  // float [2][kSoftmaxWarps][GP]
   static constexpr int kBars = align128(kRedSum + 2 * kSoftmaxWarps * GP * 4);
   static constexpr int kMaxSlots = 16;
-  static constexpr int kNumBars = 2 * kMaxSlots + 2 * kMeta + 3 * kMaxTmemBufs + 2;
+  static constexpr int kNumBars = 2 * kMaxSlots + 2 * kMeta + 3 * kMaxTmemBufs + 2 + 1;
   // tmem address (+0), abort flag (+8), item ids of the metadata slots
   // (+16, kMeta ints)
   static constexpr int kMisc = kBars + kNumBars * 8;
@@ -364,8 +373,10 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return r;
 }
 
-// Bounded wait that also gives up once another role raised the abort flag.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// Bounded wait (limit_ns of globaltimer, DecodeParams::wait_limit_ns) that
+// also gives up once another role raised the abort flag.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
@@ -374,7 +385,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
     if (*abort_flag) return false;
     uint64_t t1;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-    if (t1 - t0 > kWaitLimitNs) {
+    if (t1 - t0 > limit_ns) {
       *abort_flag = 1;  // the other roles leave their loops at their next wait
       return false;
     }
@@ -398,8 +409,10 @@ __device__ __forceinline__ void split_f16x2(__half2 x, uint16_t (&t)[nt]) {
   }
 }
 
-// Query pair (|x| < 448, bf16 values scaled by a power of two): two exact
-// E4M3 terms each, x = t0 + t1/16.
+// Query pair (|x| < 256, bf16 values scaled by a power of two): two E4M3
+// terms each, x = t0 + t1/16, exact for |x| >= 2^-6 (the residual x - t0 then
+// has at most 4 significant bits, all within E4M3's range once scaled by 16),
+// else within 2^-14.
 __device__ __forceinline__ void split_q2(float lo, float hi, uint16_t (&t)[kTermsQ]) {
   split_f16x2<kTermsQ>(__floats2half2_rn(lo, hi), t);
 }
@@ -450,6 +463,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
   uint64_t* o_full = s_full + kMaxTmemBufs;        // [kTmemBufs] MMA commit -> epilogue
   uint64_t* tmem_empty = o_full + kMaxTmemBufs;    // [kTmemBufs] epilogue (softmax threads) -> MMA
   uint64_t* p_full = tmem_empty + kMaxTmemBufs;    // [2] softmax -> MMA (Ps double buffer)
+  uint64_t* mma_drain = p_full + 2;                // MMA warp's final commit (its MMAs have completed)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMisc + 8);
   volatile int* item_ids = reinterpret_cast<volatile int*>(smem + C::kMisc + 16);  // [kMeta]
@@ -487,6 +501,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       mbar_init(tmem_empty + b, 32 * C::kSoftmaxWarps);
     }
     for (int b = 0; b < 2; ++b) mbar_init(p_full + b, C::kSoftmaxSets);
+    mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -574,7 +589,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       // metadata slot m is free once item k-kMeta is fully consumed
       const int um = k / kMeta;
       if (um > 0 &&
-          !__all_sync(0xffffffffu, wait_or_abort(meta_empty + m, (uint32_t)((um - 1) & 1), abort_flag))) {
+          !__all_sync(0xffffffffu, wait_or_abort(meta_empty + m, (uint32_t)((um - 1) & 1), abort_flag, p.wait_limit_ns))) {
         failed = true;
         break;
       }
@@ -614,8 +629,9 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     }
     // drain: the last row-map copies have landed before the warp leaves (the
     // end-of-work slot k took the slot of item k - kMeta, whose copy the
-    // consumers had already waited for)
-    for (int kk = max(0, k - kMeta + 1); kk < k; ++kk)
+    // consumers had already waited for -- unless the wait for that slot is
+    // what failed, and then item k - kMeta's copy is drained too)
+    for (int kk = max(0, k - kMeta + (failed ? 0 : 1)); kk < k; ++kk)
       if (!mbar_wait_bounded(meta_full + kk % kMeta, (uint32_t)((kk / kMeta) & 1), kWaitLimitNs)) failed = true;
   } else if (warp <= kLoaders) {
     // =============================== loaders ================================
@@ -637,8 +653,10 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         if (s % kLoaders != L) continue;
         const int fill = (pos - 1) / C::kSlots;
         if (fill > 0 &&
-            !__all_sync(0xffffffffu, wait_or_abort(kv_empty + s, (uint32_t)((fill - 1) & 1), abort_flag)))
+            !__all_sync(0xffffffffu, wait_or_abort(kv_empty + s, (uint32_t)((fill - 1) & 1), abort_flag, p.wait_limit_ns))) {
+          --pos;  // this position was not issued: the drain below counts issued fills only
           return false;
+        }
         const int4 t = *reinterpret_cast<const int4*>(tab + j * kTile + lane * 4);
         const int hkv = p.num_kv_heads;
         if (lane == 0) mbar_arrive_expect_tx(kv_full + s, kTileBytes);
@@ -654,7 +672,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     bool have_prev = false;
     for (int k = 0; !failed; ++k) {
       const int m = k % kMeta;
-      if (!__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag))) {
+      if (!__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag, p.wait_limit_ns))) {
         failed = true;
         break;
       }
@@ -693,7 +711,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       bool have_prev = false;
       for (int k = 0; !failed; ++k) {
         const int m = k % kMeta;
-        if (!wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag)) {
+        if (!wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag, p.wait_limit_ns)) {
           failed = true;
           break;
         }
@@ -703,7 +721,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
           // S(k) = K tiles of item k . Qs^T
           const int tb = k % C::kTmemBufs;
           const int ut = k / C::kTmemBufs;
-          if (ut > 0 && !wait_or_abort(tmem_empty + tb, (uint32_t)((ut - 1) & 1), abort_flag)) {
+          if (ut > 0 && !wait_or_abort(tmem_empty + tb, (uint32_t)((ut - 1) & 1), abort_flag, p.wait_limit_ns)) {
             failed = true;
             break;
           }
@@ -713,7 +731,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
           for (int j = 0; j < C::kTiles; ++j) {
             if (!((mask >> j) & 1u)) continue;
             const int slot = t % C::kSlots;
-            if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
+            if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag, p.wait_limit_ns)) {
               failed = true;
               break;
             }
@@ -737,7 +755,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
           const int jt = k - 1;
           const int pb = jt & 1;
           const int tb = jt % C::kTmemBufs;
-          if (!wait_or_abort(p_full + pb, (uint32_t)((jt >> 1) & 1), abort_flag)) {
+          if (!wait_or_abort(p_full + pb, (uint32_t)((jt >> 1) & 1), abort_flag, p.wait_limit_ns)) {
             failed = true;
             break;
           }
@@ -748,7 +766,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
           for (int j = 0; j < C::kTiles; ++j) {
             if (!((prev_mask >> j) & 1u)) continue;
             const int slot = t % C::kSlots;
-            if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag)) {
+            if (!wait_or_abort(kv_full + slot, (uint32_t)((t / C::kSlots) & 1), abort_flag, p.wait_limit_ns)) {
               failed = true;
               break;
             }
@@ -774,6 +792,13 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         prev_mask = mask;
         have_prev = true;
       }
+    }
+    // drain: every MMA this thread issued has completed (and made its commit
+    // arrivals) before TMEM is freed and the CTA exits -- immediate on the
+    // normal path, where the epilogue waited for the last one
+    if (lane == 0) {
+      mma_commit(mma_drain);
+      if (!mbar_wait_bounded(mma_drain, 0u, kWaitLimitNs)) failed = true;
     }
     // the other 31 lanes wait here for lane 0, so that the whole warp reaches
     // the CTA barrier below together (a barrier met by a diverged warp would
@@ -814,7 +839,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     auto epilogue = [&]() {
       const int tb = e_k % C::kTmemBufs;
       if (!failed)
-        failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + tb, (uint32_t)((e_k / C::kTmemBufs) & 1), abort_flag));
+        failed = !__all_sync(0xffffffffu, wait_or_abort(o_full + tb, (uint32_t)((e_k / C::kTmemBufs) & 1), abort_flag, p.wait_limit_ns));
       if (failed) return;
       tc_fence_after();
       // the O columns of this warp's heads (their kTermsP terms each)
@@ -877,7 +902,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       if constexpr (split) {
         const int m = k % kMeta;
         if (!failed)
-          failed = !__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag));
+          failed = !__all_sync(0xffffffffu, wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag, p.wait_limit_ns));
         if (bar_red_or(vote_bar, 128, failed)) {
           failed = true;
           break;
@@ -903,8 +928,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       // scores. Once anything failed the group keeps walking its items (the
       // named barriers must still match) but skips tensor memory.
       if (!failed) {
-        const bool ok = (split || wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag)) &&
-                        wait_or_abort(s_full + tb, (uint32_t)((k / C::kTmemBufs) & 1), abort_flag);
+        const bool ok = (split || wait_or_abort(meta_full + m, (uint32_t)((k / kMeta) & 1), abort_flag, p.wait_limit_ns)) &&
+                        wait_or_abort(s_full + tb, (uint32_t)((k / C::kTmemBufs) & 1), abort_flag, p.wait_limit_ns);
         failed = !__all_sync(0xffffffffu, ok);
       }
       tc_fence_after();

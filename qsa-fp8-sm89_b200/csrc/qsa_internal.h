@@ -66,7 +66,15 @@ struct DecodeParams {
   int merge_chunks;
 
   int* err;  // device error word of the current device
+  // Limit of each pipeline wait of the tensor-core kernel, in ns of
+  // globaltimer: 1 s, unless the test hook qsa_b200_testing_set_wait_limit_ns
+  // shortened it. A CTA whose wait runs out sets err and returns.
+  uint64_t wait_limit_ns;
 };
+
+// Wait limit the launches of this process use (the test hook's value, else
+// the 1 s default).
+uint64_t wait_limit_ns();
 
 // Kernel launchers (return cudaGetLastError() of the launch).
 cudaError_t launch_decode_tc(const DecodeParams& p, cudaStream_t stream);

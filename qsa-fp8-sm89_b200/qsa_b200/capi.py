@@ -55,6 +55,8 @@ EXPORTED = (
     "qsa_b200_cache_write",
     "qsa_b200_topk_select",
 )
+# test hook (include/qsa_b200_testing.h), not part of the decode interface
+TESTING_EXPORTED = ("qsa_b200_testing_set_wait_limit_ns",)
 
 
 class DecodeArgs(ctypes.Structure):
@@ -156,8 +158,27 @@ def lib() -> ctypes.CDLL:
         L.qsa_b200_cache_write.restype = c_int
         L.qsa_b200_topk_select.argtypes = [ctypes.POINTER(TopkArgs), c_void_p]
         L.qsa_b200_topk_select.restype = c_int
+        L.qsa_b200_testing_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
+        L.qsa_b200_testing_set_wait_limit_ns.restype = ctypes.c_uint64
         _configured = True
     return L
+
+
+def testing_set_wait_limit_ns(ns: int) -> int:
+    """Test hook: the limit of the tensor-core kernel's pipeline waits for
+    the launches that follow (0 = the 1 s default); returns the previous one."""
+    return int(lib().qsa_b200_testing_set_wait_limit_ns(int(ns)))
+
+
+def check_device_error(clear: bool = True) -> None:
+    """Raises RuntimeError (QSA_B200_ERR_KERNEL's text and the error word)
+    when a kernel has reported a device-side failure, such as a bounded wait
+    that ran out; clears the word first when ``clear``. Synchronous."""
+    word = device_error(clear=clear)
+    if word < 0:
+        raise RuntimeError(f"reading the device error word failed: {status_string(word)}")
+    if word != 0:
+        raise RuntimeError(f"{status_string(ERR_KERNEL)} (device error word {word})")
 
 
 def status_string(status: int) -> str:

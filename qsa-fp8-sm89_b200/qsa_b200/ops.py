@@ -155,14 +155,22 @@ def qsa_topk_select(scores, k, lengths=None, out=None):
 
     if scores.dtype != torch.float32 or scores.dim() != 2 or scores.stride(1) != 1 or not scores.is_cuda:
         raise ValueError("scores must be a CUDA float32 [rows, ctx] tensor with unit inner stride")
-    if lengths is not None and (lengths.dtype != torch.int32 or not lengths.is_contiguous()
-                                or lengths.numel() != scores.shape[0]):
-        raise ValueError("lengths must be a contiguous int32 [rows] tensor")
+    if lengths is not None:
+        if lengths.dtype != torch.int32 or not lengths.is_contiguous() or lengths.numel() != scores.shape[0]:
+            raise ValueError("lengths must be a contiguous int32 [rows] tensor")
+        if lengths.device != scores.device:
+            raise ValueError(f"lengths is on {lengths.device} but scores is on {scores.device}")
     if out is None:
         out = torch.empty(scores.shape[0], int(k), dtype=torch.int32, device=scores.device)
-    elif out.dtype != torch.int32 or out.dim() != 2 or out.stride(1) != 1 or out.shape != (scores.shape[0], int(k)):
-        raise ValueError("out must be an int32 [rows, k] tensor with unit inner stride")
-    st = capi.topk_select(capi.make_topk_args(scores, k, out, lengths), torch.cuda.current_stream().cuda_stream)
+    else:
+        if out.dtype != torch.int32 or out.dim() != 2 or out.stride(1) != 1 or out.shape != (scores.shape[0], int(k)):
+            raise ValueError("out must be an int32 [rows, k] tensor with unit inner stride")
+        if out.device != scores.device:
+            raise ValueError(f"out is on {out.device} but scores is on {scores.device}")
+    # the launch goes to the scores' device and its current stream
+    with torch.cuda.device(scores.device):
+        st = capi.topk_select(capi.make_topk_args(scores, k, out, lengths),
+                              torch.cuda.current_stream(scores.device).cuda_stream)
     if st != 0:
         raise RuntimeError(f"qsa_b200_topk_select failed: {capi.lib().qsa_b200_status_string(st).decode()}")
     return out
@@ -199,19 +207,24 @@ def chunk_tokens(num_q_heads, num_kv_heads) -> int:
     return 512
 
 
-def workspace_bytes(rows, num_q_heads, num_kv_heads, topk, kernel="auto") -> int:
+def workspace_bytes(rows, num_q_heads, num_kv_heads, topk, kernel="auto", sm_count=None) -> int:
     """Device workspace one call needs, each part 256-byte aligned: the row
     map of the tensor-core kernel (one int32 token slot per Top-K entry,
     rows x chunks x chunk entries), its tile flags (16 bytes per row and
     chunk) and its item claim counter, then, when a Top-K row spans more than
-    one chunk, the per-chunk partial outputs and log-sum-exps."""
+    one chunk and the chunks are not merged inside the decode kernel
+    (``tc_merges_chunks``), the per-chunk partial outputs and log-sum-exps.
+    ``sm_count`` defaults to the current CUDA device's (148 without one)."""
     a256 = lambda x: -(-x // 256) * 256
     c = chunk_tokens(num_q_heads, num_kv_heads)
     chunks = 1 if topk <= c else -(-topk // c)
     group = num_q_heads // num_kv_heads
     tc = kernel == "tc" or (kernel == "auto" and tc_supports_group(group))
     total = a256(rows * chunks * c * 4) + a256(rows * chunks * 16) + 256 if (tc and rows > 0) else 0
-    if chunks > 1:
+    if sm_count is None:
+        sm_count = (torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+                    if torch.cuda.is_available() else 148)
+    if chunks > 1 and not (tc and tc_merges_chunks(rows, num_q_heads, num_kv_heads, topk, sm_count)):
         n = rows * num_q_heads * chunks
         total += a256(n * 128 * 4) + a256(n * 4)
     return total

@@ -32,6 +32,18 @@ def golden():
     return {name: load_golden(name) for name in GOLDEN_CASES}
 
 
+def fp32_floor(z: dict) -> float:
+    """Absolute error floor of an fp32 evaluation of a fixture's softmax
+    average: K accumulated terms of at most max|V| * v_scale each, one fp32
+    rounding (2^-24) apiece (at least 1e-6). The reference's own torch_eager
+    and reference() disagree by about that where the output cancels to near
+    zero, as in the dynamic-range case."""
+    from oracle import qsa_oracle as O
+
+    vmax = float(np.nanmax(np.abs(O.e4m3fn_table()[z["v"]]))) * float(z["v_scale"])
+    return max(1e-6, z["indices"].shape[1] * 2.0 ** -24 * vmax)
+
+
 def bf16_ulp(x: np.ndarray) -> np.ndarray:
     """Spacing of bf16 numbers around |x| (2^(floor(log2|x|) - 7))."""
     a = np.abs(np.asarray(x, dtype=np.float64))

@@ -1,10 +1,10 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
-Run once in a container that has the reference checkout (``$QSA_REFERENCE_DIR``
-or the default of ``--reference-dir``) and the ``cutlass`` DSL package, which
-``sm89_cutedsl`` imports at module level:
+Run once in a container that has the reference checkout (given as
+``--reference-dir`` or ``$QSA_REFERENCE_DIR``) and the ``cutlass`` DSL
+package, which ``sm89_cutedsl`` imports at module level:
 
-    python tests/golden/make_golden.py [--reference-dir DIR]
+    python tests/golden/make_golden.py --reference-dir DIR [--only CASE ...]
 
 It imports the reference's own ``sm89_torch.torch_eager`` (sm89_torch.py:27-54)
 and ``sm89_cutedsl.reference`` (sm89_cutedsl.py:83-116), sets the module globals
@@ -19,6 +19,15 @@ length ``pages_per_req * P`` and uses ``num_pages == B * pages_per_req``.
 ``reference`` reads the valid count from an extra last column of ``indices``
 (sm89_cutedsl.py:87, :92); the fixtures store indices ``[B, K]`` and counts
 ``[B]`` separately and append the column only for that call.
+
+Two cases come from the reference's own generator, ``make_tensors``
+(sm89_cutedsl.py:43-79), called with its shape globals shrunk: seed 42, K/V
+``bf16 randn * 0.1`` cast to E4M3FN (most bytes in the smallest exponents and
+the subnormals), an identity block table, sequential indices with the count
+in the last column, and ``k_scale = v_scale = 0.1``. ``range`` stresses the
+dynamic range of the FP8 term splits: one query element per head far above
+the others and K/V spread out to +-448, so that the probabilities span many
+decades.
 """
 
 from __future__ import annotations
@@ -108,7 +117,41 @@ def _paged_case(seed, b, hq, hkv, d, p, ppr, topk, kv_std=1.0, sample=False,
                 indices=indices, counts=counts, k_scale=k_scale, v_scale=v_scale)
 
 
-def cases():
+def _make_tensors_case(mods, rows, topk):
+    """The reference's own fixture generator with shrunk globals."""
+    sm89_cutedsl = mods[1]
+    g = dict(NUM_REQUESTS=rows, NUM_Q_HEADS=32, NUM_KV_HEADS=8, GROUP_SIZE=4, HEAD_DIM=128, PAGE_SIZE=16,
+             TOPK=topk, MAX_PAGES=topk // 16)
+    for name, val in g.items():
+        setattr(sm89_cutedsl, name, val)
+    q, k, v, ks, vs, btable, t2r, idx, gate = sm89_cutedsl.make_tensors("cpu")
+    return dict(q=q, k=k, v=v, gate=gate, btable=btable, t2r=t2r, indices=idx[:, :topk].contiguous(),
+                counts=idx[:, topk].contiguous(), k_scale=float(ks), v_scale=float(vs))
+
+
+def _range_case(seed):
+    """FP8 dynamic-range stress: per head, one query element 2^14 (about
+    1.6e4) times the others' scale; K/V ~ N(0, 150) clamped to +-448 (a
+    quarter of the bytes at the top exponents); k_scale 0.05, so that a
+    head's scores spread over about +-16 and its probabilities over about 14
+    decades; one row with V at +-448 everywhere."""
+    c = _paged_case(seed, b=3, hq=32, hkv=8, d=128, p=16, ppr=4, topk=64, kv_std=150.0, k_scale=0.05,
+                    v_scale=0.5)
+    gen = torch.Generator().manual_seed(seed + 1)
+    b, hq, d = c["q"].shape
+    q = torch.randn(b, hq, d, generator=gen) * 5e-4
+    big = torch.randint(0, d, (b, hq), generator=gen)
+    q[torch.arange(b)[:, None], torch.arange(hq)[None, :], big] = 8.0 * torch.sign(torch.randn(b, hq, generator=gen))
+    c["q"] = q.to(torch.bfloat16)
+    v = c["v"].view(torch.uint8).clone()
+    pages = c["btable"][2].long()
+    sign = (torch.rand(pages.numel(), 16, 8, d, generator=gen) < 0.5).to(torch.uint8) << 7
+    v[pages] = 0x7E | sign  # +-448
+    c["v"] = v.view(torch.float8_e4m3fn)
+    return c
+
+
+def cases(mods=None):
     out = {}
     # configs[0]: the reference's CPU-runnable case, B=4, 4 pages/request,
     # Top-K 64 = every token in random order, 16 shuffled pages.
@@ -153,15 +196,26 @@ def cases():
     kat["k"] = torch.full_like(kat["k"].view(torch.uint8), 0x38).view(torch.float8_e4m3fn)
     kat["v"] = kat["k"].clone()
     out["kat"] = kat
+
+    if mods is not None:
+        # the reference's own generator (sm89_cutedsl.py:43-79)
+        out["mt_small"] = _make_tensors_case(mods, rows=4, topk=64)
+        out["mt_tile"] = _make_tensors_case(mods, rows=2, topk=256)
+    out["range"] = _range_case(11)
     return out
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-dir", default=os.environ.get("QSA_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--reference-dir", default=os.environ.get("QSA_REFERENCE_DIR"))
+    ap.add_argument("--only", nargs="*", help="write only these cases (default: all)")
     args = ap.parse_args()
+    if not args.reference_dir:
+        ap.error("give the reference checkout as --reference-dir or $QSA_REFERENCE_DIR")
     mods = _load_reference(args.reference_dir)
-    for name, c in cases().items():
+    for name, c in cases(mods).items():
+        if args.only and name not in args.only:
+            continue
         eager, loop = _run_reference(mods, c)
         np.savez_compressed(
             HERE / f"{name}.npz",

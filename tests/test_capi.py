@@ -13,10 +13,11 @@ import torch
 from conftest import PKG_ROOT, REPO
 
 HEADER = REPO / "include" / "qsa_b200.h"
+HEADERS = sorted((REPO / "include").glob("*.h"))
 
 
-def _declared_functions():
-    text = HEADER.read_text()
+def _declared_functions(headers=None):
+    text = "\n".join(h.read_text() for h in (headers or HEADERS))
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     names = re.findall(r"^\s*(?:[A-Za-z_][\w\s\*]*?)\b([A-Za-z_]\w*)\s*\(", text, flags=re.M)
     return sorted({n for n in names if n not in ("if", "defined")})
@@ -34,7 +35,8 @@ def test_library_exports_every_declared_symbol():
     declared = _declared_functions()
     for name in declared:
         assert hasattr(lib, name), name
-    assert set(declared) == set(capi.EXPORTED)
+    assert set(declared) == set(capi.EXPORTED) | set(capi.TESTING_EXPORTED)
+    assert set(_declared_functions([HEADER])) == set(capi.EXPORTED)
     assert lib.qsa_b200_abi_version() == 1
 
 
@@ -82,6 +84,11 @@ def _args_cpu(**over):
     (dict(btable_stride=2), -2),
     (dict(kernel=7), -3),
     (dict(num_q_heads=72, kernel=1), -3),  # G = 9: odd above 8 runs on the CUDA-core kernel only
+    # tensor-core kernel limits: 2^24 pages x 16 x 8 KV heads = 2^31 rows of
+    # 128 bytes; 2^24 rows x 8 KV heads x 8 chunks = 2^30 work items
+    (dict(num_pages=1 << 24), -3),
+    (dict(num_pages=1 << 24, kernel=1), -3),
+    (dict(rows=1 << 24, num_reqs=1 << 24, topk=4096, indices_stride=4096), -3),
 ])
 def test_validation_errors(over, code):
     from qsa_b200 import capi
@@ -138,6 +145,16 @@ def test_workspace_sizes():
     a.num_q_heads = 72  # group 9: CUDA-core kernel, no row map
     n = 4 * 72 * 3
     assert capi.workspace_bytes(a) == n * 512 + a256(n * 4) == ops.workspace_bytes(4, 72, 8, 1100)
+    # enough (row, KV head) pairs for the decode kernel to merge the chunks
+    # itself (at least two per SM): no partials
+    a.num_q_heads, a.rows, a.num_reqs = 32, 1024, 1024
+    a.num_pages = 1024 * a.pages_per_req
+    rowmap = 1024 * 3 * 512 * 4 + a256(1024 * 3 * 16) + 256
+    assert capi.workspace_bytes(a) == rowmap == ops.workspace_bytes(1024, 32, 8, 1100, sm_count=148)
+    a.kernel = capi.KERNEL_SIMT  # the CUDA-core kernel always writes partials
+    n = 1024 * 32 * 3
+    assert capi.workspace_bytes(a) == n * 512 + a256(n * 4) == ops.workspace_bytes(1024, 32, 8, 1100,
+                                                                                     kernel="simt")
 
 
 def test_torch_ops_register_and_refuse_cpu_tensors():

@@ -113,3 +113,52 @@ def test_two_rank_gloo_shard_compute_gather(tmp_path):
     got, ref = np.load(out)
     assert got.shape == ref.shape == (6, 8, 128)
     np.testing.assert_array_equal(got, ref)
+
+
+def _plan_rank_main(rank, world, port, out_path):
+    """One rank of the bench's plan: its requests of configs[3] and [4] and
+    the config object its line would carry, gathered on every rank."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+
+        mine = {cfg: bench.rank_rows(cfg, rank, world)[1] for cfg in (3, 4)}
+        conf = {cfg: bench.bench_config(cfg, world, *bench.config_rows(cfg, world)) for cfg in (1, 3, 4)}
+        everyone = bench.gather_objects({"rows": mine, "config": conf}, world)
+        if rank == 0:
+            import json
+
+            with open(out_path, "w") as f:
+                json.dump(everyone, f)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_bench_plan_over_gloo_ranks(tmp_path, world):
+    """configs[3]: contiguous ranges covering the 2048 requests once;
+    LPT bins covering the 1024 ragged requests once, each bin's
+    Top-K entries within one request of the mean; every rank prints the same
+    ``config``."""
+    import json
+
+    from qsa_b200.inputs import CONFIGS, ragged_lengths
+
+    out = tmp_path / "plan.json"
+    mp.start_processes(_plan_rank_main, args=(world, _free_port(), str(out)), nprocs=world, join=True,
+                       start_method="spawn")
+    everyone = json.loads(out.read_text())
+    assert len(everyone) == world
+    rows3 = [r["rows"]["3"] for r in everyone]
+    assert [i for rr in rows3 for i in rr] == list(range(2048))
+    rows4 = [r["rows"]["4"] for r in everyone]
+    assert sorted(i for rr in rows4 for i in rr) == list(range(1024))
+    lengths = ragged_lengths(CONFIGS[4], 1024, seed=0)
+    loads = [int(lengths[rr].sum()) for rr in rows4]
+    assert max(loads) - sum(loads) / world <= int(lengths.max())
+    assert all(r["config"] == everyone[0]["config"] for r in everyone)
+    assert everyone[0]["config"]["3"]["rows_per_gpu"] == 2048 // world
+    assert everyone[0]["config"]["1"]["rows_total"] == 256 * world

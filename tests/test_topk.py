@@ -42,6 +42,12 @@ def _scores(rows, ctx, kind, seed):
         s = torch.randint(0, 8, (rows, ctx), generator=g).float()
     else:
         s = torch.randn(rows, ctx, generator=g)
+    if kind == "subnormal":
+        # float32 subnormals of both signs with many ties, +0 and -0 mixed
+        s = torch.randint(-3, 4, (rows, ctx), generator=g).float() * 1e-42
+        zero = s == 0
+        flip = torch.rand(rows, ctx, generator=g) < 0.5
+        s[zero & flip] = -0.0
     if kind == "special":
         m = torch.rand(rows, ctx, generator=g)
         s[m < 0.05] = float("-inf")
@@ -55,6 +61,8 @@ def _scores(rows, ctx, kind, seed):
 @pytest.mark.parametrize("rows,ctx,k,kind", [
     (5, 1000, 17, "randn"), (4, 4096, 512, "ties"), (3, 5000, 2048, "special"),
     (2, 32768, 2048, "randn"), (3, 2048, 2048, "ties"), (6, 300, 1, "special"), (2, 64, 100, "randn"),
+    (4, 5000, 1500, "subnormal"), (3, 700, 300, "subnormal"), (1, (1 << 20) - 3, 2048, "randn"),
+    (1, 1 << 20, 2048, "ties"),
 ])
 def test_kernel_matches_oracle(rows, ctx, k, kind):
     import torch
@@ -107,3 +115,28 @@ def test_produced_indices_feed_the_decode():
     ref = O.attention(bits(w.q), u8(w.k).reshape(w.k.shape), u8(w.v).reshape(w.v.shape), 1.0, 1.0,
                       w.btable.cpu().numpy(), w.t2r.cpu().numpy(), ref_idx, bits(w.gate))
     check_close(bits(out), ref, what="topk -> decode")
+
+
+def test_oracle_orders_subnormals_and_signed_zeros():
+    """Subnormal scores order by value, and -0 ties +0 (lower position wins)."""
+    d = np.float32(1e-42)
+    s = np.array([[0.0, -0.0, d, -d, 2 * d, -0.0, 0.0]], dtype=np.float32)
+    assert O.topk_select(s, 1).tolist() == [[4]]
+    assert O.topk_select(s, 2).tolist() == [[2, 4]]
+    # the third-highest score is 0: positions 0 and 1 (+0, -0) win over 5, 6
+    assert O.topk_select(s, 4).tolist() == [[0, 1, 2, 4]]
+
+
+@pytest.mark.gpu
+def test_rejects_tensors_on_another_device():
+    """lengths / out must live on the scores' device (a host pointer handed to
+    the kernel would fault it)."""
+    import torch
+
+    from qsa_b200 import qsa_topk_select
+
+    s = torch.randn(2, 100, device="cuda")
+    with pytest.raises(ValueError, match="lengths"):
+        qsa_topk_select(s, 5, lengths=torch.full((2,), 50, dtype=torch.int32))
+    with pytest.raises(ValueError, match="out"):
+        qsa_topk_select(s, 5, out=torch.empty(2, 5, dtype=torch.int32))

@@ -61,7 +61,8 @@ def test_noalloc_matches_decode_on_two_consecutive_calls(name):
 
 def test_noalloc_rejects_a_split_above_its_fixed_scratch():
     """Refused before any device call, so this runs without a GPU: 1024 rows x
-    32 query heads x 4 chunks needs about 67 MB of split scratch."""
+    128 query heads (group 16, whose chunks are never merged inside the decode
+    kernel) x 4 chunks need about 270 MB of split partials."""
     from qsa_b200 import capi
 
     a = capi.DecodeArgs()
@@ -69,7 +70,7 @@ def test_noalloc_rejects_a_split_above_its_fixed_scratch():
     for f in ("q", "k_cache", "v_cache", "indices", "btable", "gate", "out"):
         setattr(a, f, ctypes.c_void_p(fake))
     a.softmax_scale, a.k_scale, a.v_scale = 128 ** -0.5, 1.0, 1.0
-    a.rows, a.num_q_heads, a.num_kv_heads, a.head_dim = 1024, 32, 8, 128
+    a.rows, a.num_q_heads, a.num_kv_heads, a.head_dim = 1024, 128, 8, 128
     a.page_size, a.pages_per_req, a.num_reqs, a.num_pages = 16, 128, 1024, 1024 * 128
     a.topk, a.indices_stride, a.count_column, a.btable_stride = 2048, 2048, 0, 128
     a.kernel = capi.KERNEL_AUTO
