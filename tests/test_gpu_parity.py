@@ -63,13 +63,33 @@ def test_golden_vs_reference_outputs(golden, name, kernel):
 
 
 @pytest.mark.parametrize("kernel", KERNELS)
-@pytest.mark.parametrize("name", GOLDEN_CASES)
+@pytest.mark.parametrize("name", [n for n in GOLDEN_CASES if n != "range"])
 def test_golden_vs_oracle_tight(golden, name, kernel):
     """Beyond the 2e-2 gate: within one bf16 step (plus 2e-5) of the float64
     oracle."""
     z = golden[name]
     out = _decode(np_to_dev(z), kernel, counts=True)
     assert max_ulps(bits(out), _oracle_np(z)) <= 1.0
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_dynamic_range_case_within_the_term_split_bound(golden, kernel):
+    """The dynamic-range fixture (one query element per head 2^14 above the
+    others, K/V spread to +-448, probabilities over about 14 decades). The
+    tensor-core kernel's FP8 term splits carry each probability to about 15
+    significant bits and leave query elements below 2^-13 of their head's
+    largest with an absolute error under 2^-21 of it, so its bound beyond one
+    bf16 step is 2^-15 of the largest |V * v_scale| (6.8e-3 here; measured
+    about 1e-3). The CUDA-core kernel computes in fp32 and stays within one
+    step plus the fp32 accumulation floor."""
+    from conftest import fp32_floor
+    from oracle import qsa_oracle as O
+
+    z = golden["range"]
+    out = _decode(np_to_dev(z), kernel, counts=True)
+    vmax = float(np.nanmax(np.abs(O.e4m3fn_table()[z["v"]]))) * float(z["v_scale"])
+    floor = 2.0 ** -15 * vmax if kernel == "tc" else fp32_floor(z)
+    assert max_ulps(bits(out), _oracle_np(z), abs_floor=floor) <= 1.0
 
 
 def test_kat_closed_form_through_run(golden):

@@ -19,11 +19,12 @@ from gpu_helpers import bits, check_close, oracle_subset
 pytestmark = pytest.mark.gpu
 
 # (workload config, overrides, rows): unsplit rows (the static item walk),
-# split rows whose chunks go out as partials to the combine kernel, and split
-# rows merged inside the CTA (the claimed walk with its named-barrier votes)
+# split rows whose chunks go out as partials to the combine kernel (fewer than
+# two (row, KV head) pairs per SM: 32 rows x 8 KV heads), and split rows
+# merged inside the CTA (the claimed walk with its named-barrier votes)
 SHAPES = {
     "unsplit": (1, {}, 64),
-    "split_partials": (0, dict(ppr=100, topk=1500, mode="sample"), 64),
+    "split_partials": (0, dict(ppr=100, topk=1500, mode="sample"), 32),
     "split_merged": (4, dict(ppr=160, topk=2048, len_lo=64, len_hi=2048), 320),
 }
 
