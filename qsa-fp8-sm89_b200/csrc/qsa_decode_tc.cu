@@ -1218,6 +1218,13 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
     e = cudaFuncSetAttribute(qsa_decode_tc_kernel<G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmemAlloc);
     if (e != cudaSuccess) return e;
+    // the row-map kernel asks for the decode's shared-memory carveout, so
+    // that the decode CTAs (its programmatic dependents) start, and run their
+    // prologue, on SMs that still hold row-map blocks instead of waiting for
+    // those to leave
+    e = cudaFuncSetAttribute(qsa_rowmap_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   const int64_t items = (int64_t)p.rows * p.num_kv_heads * p.num_chunks;
