@@ -48,6 +48,16 @@ def _scores(rows, ctx, kind, seed):
         zero = s == 0
         flip = torch.rand(rows, ctx, generator=g) < 0.5
         s[zero & flip] = -0.0
+    if kind.startswith("bucket"):
+        # 1000 scores above the threshold bucket, then n keys sharing the top
+        # 11 key bits of 1.5 (the bucket holding the k-th score: exactly the
+        # kernel's shared-memory candidate buffer at n = 8192, one past it at
+        # 8193), the rest far below, in random positions
+        n = int(kind[len("bucket"):])
+        v = torch.cat([100.0 + torch.randperm(1000, generator=g).float(),
+                       1.5 + 0.2 * torch.rand(n, generator=g),
+                       -10.0 - torch.rand(ctx - 1000 - n, generator=g)])
+        s = torch.stack([v[torch.randperm(ctx, generator=g)] for _ in range(rows)])
     if kind == "special":
         m = torch.rand(rows, ctx, generator=g)
         s[m < 0.05] = float("-inf")
@@ -62,7 +72,8 @@ def _scores(rows, ctx, kind, seed):
     (5, 1000, 17, "randn"), (4, 4096, 512, "ties"), (3, 5000, 2048, "special"),
     (2, 32768, 2048, "randn"), (3, 2048, 2048, "ties"), (6, 300, 1, "special"), (2, 64, 100, "randn"),
     (4, 5000, 1500, "subnormal"), (3, 700, 300, "subnormal"), (1, (1 << 20) - 3, 2048, "randn"),
-    (1, 1 << 20, 2048, "ties"),
+    (1, 1 << 20, 2048, "ties"), (2, 32768, 2048, "bucket8192"), (2, 32768, 2048, "bucket8193"),
+    (2, 32771, 2048, "bucket8192"),
 ])
 def test_kernel_matches_oracle(rows, ctx, k, kind):
     import torch
