@@ -58,6 +58,12 @@ def _scores(rows, ctx, kind, seed):
                        1.5 + 0.2 * torch.rand(n, generator=g),
                        -10.0 - torch.rand(ctx - 1000 - n, generator=g)])
         s = torch.stack([v[torch.randperm(ctx, generator=g)] for _ in range(rows)])
+    if kind == "sorted":
+        s = torch.sort(s, dim=1).values
+    if kind.startswith("strided"):
+        # every 32nd score far below (or above) the rest: a strided sample of
+        # the row sees a distribution unlike the row's
+        s[:, ::32] = -50.0 if kind == "strided_low" else 50.0 + s[:, ::32]
     if kind == "special":
         m = torch.rand(rows, ctx, generator=g)
         s[m < 0.05] = float("-inf")
@@ -73,7 +79,9 @@ def _scores(rows, ctx, kind, seed):
     (2, 32768, 2048, "randn"), (3, 2048, 2048, "ties"), (6, 300, 1, "special"), (2, 64, 100, "randn"),
     (4, 5000, 1500, "subnormal"), (3, 700, 300, "subnormal"), (1, (1 << 20) - 3, 2048, "randn"),
     (1, 1 << 20, 2048, "ties"), (2, 32768, 2048, "bucket8192"), (2, 32768, 2048, "bucket8193"),
-    (2, 32771, 2048, "bucket8192"),
+    (2, 32771, 2048, "bucket8192"), (2, 32768, 2048, "sorted"), (2, 32768, 2048, "strided_low"),
+    (2, 32768, 2048, "strided_high"), (3, 65536, 4096, "randn"), (2, 65540, 64, "randn"),
+    (2, 1000, 1000, "randn"), (2, 1500, 1499, "ties"),
 ])
 def test_kernel_matches_oracle(rows, ctx, k, kind):
     import torch
