@@ -147,9 +147,17 @@ __device__ __forceinline__ int block_scan(int v, int* warp_sums, int& total) {
   return before;
 }
 
+// Selection state of the sampled path, identical in every thread: the key
+// prefix found so far, its mask, and the rank still wanted inside it (-1:
+// fewer keys than the rank).
+struct Sel {
+  uint32_t prefix, mask;
+  int need;
+};
+
 struct TopkShared {
   int hist[2][2048];                      // radix path: hist[0]; sampled path: both, alternately
-  int wsum[2][kTopkWarps];                // sampled path: per-warp bin-group counts
+  Sel sel_state;                          // sampled path: the state warp 0 publishes
   int warp_sums[kTopkWarps];
   uint32_t cand[kBuffer];                 // keys: >= L (sampled path), of the threshold bucket (radix path)
   int32_t cand_pos[kBuffer];              // positions of the sampled path's keys
@@ -365,38 +373,23 @@ __device__ __forceinline__ void radix_path(TopkShared& sh, const float* sc, int 
 
 
 // ---- the sampled path's selection: two barriers a digit ---------------------
-// Selection state, identical in every thread: the key prefix found so far,
-// its mask, and the rank still wanted inside it (-1: fewer keys than the
-// rank). Every warp finds each digit itself from the shared histogram (warp
-// sums over 32 groups of bins, then the bins of the group holding the rank),
-// so no block-wide scan or broadcast is needed.
-struct Sel {
-  uint32_t prefix, mask;
-  int need;
-};
-
-// Step A of a digit, after the barrier that completes histogram H (nb bins):
-// warp w writes the count of bins [w*nb/32, (w+1)*nb/32) to W[w], and the
-// CTA zeroes the other histogram Z for the next digit.
-__device__ __forceinline__ void digit_sums(const int* H, int* W, int* Z, int nb) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gs = nb / 32;  // 64 or 32 bins a group
-  int c = 0;
-  for (int i = lane; i < gs; i += 32) c += H[warp * gs + i];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-  if (lane == 0) W[warp] = c;
-  for (int b = tid; b < 2048; b += kTopkThreads) Z[b] = 0;
-}
-
-// Step B, after the barrier that completes W: the digit (bits shift ..) of
-// the rank-s.need key among the keys matching s.prefix; `first`: a total
-// below the rank sets need to -1.
-__device__ __forceinline__ Sel digit_find(const int* H, const int* W, Sel s, int nb, int shift, bool first) {
+// Warp 0 finds the digit of the rank-s.need key (bits shift .. of the keys
+// matching s.prefix) from histogram H (nb bins): each lane sums one group of
+// nb/32 bins (the groups from the top, lane l holding group 31 - l; reads
+// rotated by lane, so the 16-byte loads spread over the banks), a warp scan
+// finds the group, a second the bin. `first`: a total below the rank sets
+// need to -1.
+__device__ __forceinline__ Sel warp_find(const int* H, Sel s, int nb, int shift, bool first) {
   const int lane = threadIdx.x & 31;
   if (s.need < 0) return s;
-  // groups from the top: lane l holds group 31 - l
-  const int wc = W[31 - lane];
+  const int gs = nb / 32;  // 64 or 32 bins a group
+  const int4* hp = reinterpret_cast<const int4*>(H + (31 - lane) * gs);
+  int wc = 0;
+#pragma unroll 2
+  for (int i = 0; i < gs / 4; ++i) {
+    const int4 q = hp[(i + lane) & (gs / 4 - 1)];
+    wc += q.x + q.y + q.z + q.w;
+  }
   int cum = wc;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -410,9 +403,8 @@ __device__ __forceinline__ Sel digit_find(const int* H, const int* W, Sel s, int
   }
   const int lg = __ffs(__ballot_sync(0xffffffffu, cum >= s.need)) - 1;
   const int g = 31 - lg;
-  const int need = s.need - (__shfl_sync(0xffffffffu, cum - wc, lg));  // rank inside group g
+  const int need = s.need - __shfl_sync(0xffffffffu, cum - wc, lg);  // rank inside group g
   // bins of group g from the top: two a lane (64-bin groups) or one
-  const int gs = nb / 32;
   const int b0 = g * gs + gs - 1 - (gs == 64 ? 2 * lane : lane);
   const int c0 = H[b0];
   const int c1 = gs == 64 ? H[b0 - 1] : 0;
@@ -427,17 +419,32 @@ __device__ __forceinline__ Sel digit_find(const int* H, const int* W, Sel s, int
   const int d0 = __shfl_sync(0xffffffffu, b0, lb);
   const int k0 = __shfl_sync(0xffffffffu, c0, lb);
   const bool hi = before + k0 >= need;
-  const uint32_t dmask = (uint32_t)nb - 1u;
   s.prefix |= (uint32_t)(hi ? d0 : d0 - 1) << shift;
-  s.mask |= dmask << shift;
+  s.mask |= ((uint32_t)nb - 1u) << shift;
   s.need = need - (hi ? before : before + k0);
   return s;
 }
 
+// After the barrier that completes histogram H: warp 0 finds the digit and
+// publishes the new state, the other warps zero histogram Z for the next
+// digit. Ends with a barrier; returns the state in every thread.
+__device__ __forceinline__ Sel digit_step(TopkShared& sh, const int* H, int* Z, Sel s, int nb, int shift,
+                                          bool first) {
+  const int tid = threadIdx.x;
+  if (tid < 32) {
+    const Sel r = warp_find(H, s, nb, shift, first);
+    if (tid == 0) sh.sel_state = r;
+  } else {
+    for (int b = tid - 32; b < 2048; b += kTopkThreads - 32) Z[b] = 0;
+  }
+  __syncthreads();
+  return sh.sel_state;
+}
+
 // One digit over n keys of shared memory (histogram into H, which is zero;
 // zeroes Z). Starts after the barrier that made the keys and H ready.
-__device__ __forceinline__ Sel digit_over(const uint32_t* keys, int n, int* H, int* W, int* Z, Sel s, int nb,
-                                          int shift, bool first) {
+__device__ __forceinline__ Sel digit_over(TopkShared& sh, const uint32_t* keys, int n, int* H, int* Z, Sel s,
+                                          int nb, int shift, bool first) {
   const uint32_t dmask = (uint32_t)nb - 1u;
   if (s.need >= 0)
     for (int i = threadIdx.x; i < n; i += kTopkThreads) {
@@ -445,9 +452,7 @@ __device__ __forceinline__ Sel digit_over(const uint32_t* keys, int n, int* H, i
       if (key != 0u && (key & s.mask) == s.prefix) atomicAdd(&H[(key >> shift) & dmask], 1);
     }
   __syncthreads();
-  digit_sums(H, W, Z, nb);
-  __syncthreads();
-  return digit_find(H, W, s, nb, shift, first);
+  return digit_step(sh, H, Z, s, nb, shift, first);
 }
 
 // Valid positions of a row (its length, clamped to [0, ctx]).
@@ -496,9 +501,9 @@ __device__ __forceinline__ void topk_row(TopkShared& sh, const TopkParams& p, in
     const float q = fminf(fmaxf(1.0f - (float)k / (float)len, 0.0f), 1.0f);
     Sel s{0u, 0u, (int)fminf(ceilf(e + 6.0f * sqrtf(e * q) + 8.0f), (float)(n_s + 1))};
     __syncthreads();
-    s = digit_over(sh.cand, n_s, H0, sh.wsum[0], H1, s, 2048, 21, true);
+    s = digit_over(sh, sh.cand, n_s, H0, H1, s, 2048, 21, true);
     if (kSampleDigits == 2) {
-      s = digit_over(sh.cand, n_s, H1, sh.wsum[1], H0, s, 2048, 10, false);
+      s = digit_over(sh, sh.cand, n_s, H1, H0, s, 2048, 10, false);
     } else {
       int* const h = H0;  // H1 is the zeroed one
       H0 = H1;
@@ -562,11 +567,9 @@ __device__ __forceinline__ void topk_row(TopkShared& sh, const TopkParams& p, in
     sampled = n >= k && n <= kBuffer;  // uniform
     if (sampled) {
       // ---- 3. T from the buffer; selected positions into the bitmap -------------
-      digit_sums(H0, sh.wsum[0], H1, 2048);
-      __syncthreads();
-      s = digit_find(H0, sh.wsum[0], Sel{0u, 0u, k}, 2048, 21, true);
-      s = digit_over(sh.cand, n, H1, sh.wsum[1], H0, s, 2048, 10, false);
-      s = digit_over(sh.cand, n, H0, sh.wsum[0], H1, s, 1024, 0, false);
+      s = digit_step(sh, H0, H1, Sel{0u, 0u, k}, 2048, 21, true);
+      s = digit_over(sh, sh.cand, n, H1, H0, s, 2048, 10, false);
+      s = digit_over(sh, sh.cand, n, H0, H1, s, 1024, 0, false);
       const uint32_t T = s.prefix;
       const int take_eq = s.need;
       for (int i0 = 0; i0 < n; i0 += kTopkThreads) {
