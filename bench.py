@@ -91,8 +91,10 @@ FALLBACK_HBM_GBS = 6650.0
 # workload, from an ncu capture (not measured by this run): (bytes, which
 # capture). None where no capture of the kernel exists.
 NCU_TRAFFIC = {
-    ("configs[1]", "tc"): (278_676_480, "ncu --set full capture of one qsa_decode_tc_kernel<4,0> launch at "
-                                        "configs[1], clean caches; not measured by this run"),
+    ("configs[1]", "tc"): (277_858_816, "ncu --set full capture of one qsa_decode_tc_kernel<4,0> launch at "
+                                        "configs[1] on the current build, clean caches; not measured by this run"),
+    ("topk", None): (139_966_976, "ncu --set full capture of one qsa_topk_kernel launch at 1024 x 32768, k = 2048, "
+                                  "clean caches; not measured by this run"),
     ("cache write", 1): (772_670_000, "ncu capture of one qsa_cache_write_kernel launch on the configs[1] "
                                       "cache; not measured by this run"),
 }
@@ -971,7 +973,8 @@ def run_topk(args):
         "data": "synthetic",
         "config": {"workload": "Top-K of configs[4]'s shape", "rows": rows, "ctx": ctx, "k": k, "l2": L2_NOTE},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                     "peak_source": peak_kind, "traffic": None, "kernel": "qsa_topk_kernel",
+                     "peak_source": peak_kind, "traffic": NCU_TRAFFIC[("topk", None)][0],
+                     "traffic_source": NCU_TRAFFIC[("topk", None)][1], "kernel": "qsa_topk_kernel",
                      "bytes_per_step": moved},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
