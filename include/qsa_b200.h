@@ -65,8 +65,8 @@ enum {
 };
 
 /* Kernel selection. AUTO picks the tensor-core kernel for group sizes
- * (Hq / Hkv) 1 to 8 and 10, 12, 14, 16, and the CUDA-core kernel for the
- * others (up to 32). The tensor-core kernel (explicit or through AUTO)
+ * (Hq / Hkv) 1 to 16, and the CUDA-core kernel for the larger ones (up to
+ * 32). The tensor-core kernel (explicit or through AUTO)
  * returns QSA_B200_ERR_UNSUPPORTED for a cache of more than 2^31 - 1 rows of
  * 128 bytes (num_pages * page_size * num_kv_heads; 256 GiB per cache) and
  * for more than 2^30 - 1 work items (rows * num_kv_heads * ceil(topk / 512)). */

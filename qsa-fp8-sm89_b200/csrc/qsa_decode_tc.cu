@@ -1263,7 +1263,7 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
 int tc_chunk_tokens(int) { return 4 * kTile; }
 
 bool tc_supports_group(int group) {
-  return (group >= 1 && group <= 8) || (group <= 16 && group % 2 == 0);
+  return group >= 1 && group <= kMaxGroupTc;
 }
 
 // Split rows merge in the CTA when there are enough (row, KV head) pairs to
@@ -1289,9 +1289,13 @@ cudaError_t launch_decode_tc(const DecodeParams& params, cudaStream_t stream) {
     case 6: return launch_g<6>(p, stream);
     case 7: return launch_g<7>(p, stream);
     case 8: return launch_g<8>(p, stream);
+    case 9: return launch_g<9>(p, stream);
     case 10: return launch_g<10>(p, stream);
+    case 11: return launch_g<11>(p, stream);
     case 12: return launch_g<12>(p, stream);
+    case 13: return launch_g<13>(p, stream);
     case 14: return launch_g<14>(p, stream);
+    case 15: return launch_g<15>(p, stream);
     case 16: return launch_g<16>(p, stream);
     default: return cudaErrorInvalidValue;
   }

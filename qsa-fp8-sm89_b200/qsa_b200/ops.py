@@ -187,9 +187,9 @@ def token_slots(btable, reqs, positions, page_size):
 
 
 def tc_supports_group(group: int) -> bool:
-    """Group sizes (Hq / Hkv) of the tensor-core kernel: 1 to 8 and the even
-    sizes up to 16 (the others run on the CUDA-core kernel)."""
-    return 1 <= group <= 8 or (group <= 16 and group % 2 == 0)
+    """Group sizes (Hq / Hkv) of the tensor-core kernel: 1 to 16 (larger ones,
+    up to 32, run on the CUDA-core kernel)."""
+    return 1 <= group <= 16
 
 
 def tc_merges_chunks(rows: int, num_q_heads: int, num_kv_heads: int, topk: int, sm_count: int) -> bool:
