@@ -65,8 +65,9 @@ enum {
 };
 
 /* Kernel selection. AUTO picks the tensor-core kernel for group sizes
- * (Hq / Hkv) 1 to 16, and the CUDA-core kernel for the larger ones (up to
- * 32). The tensor-core kernel (explicit or through AUTO)
+ * (Hq / Hkv) 1 to 16 and the even ones up to 32 (each KV head's query heads
+ * in two halves, each half reading the KV rows), and the CUDA-core kernel for
+ * the odd ones from 17 to 31. The tensor-core kernel (explicit or through AUTO)
  * returns QSA_B200_ERR_UNSUPPORTED for a cache of more than 2^31 - 1 rows of
  * 128 bytes (num_pages * page_size * num_kv_heads; 256 GiB per cache) and
  * for more than 2^30 - 1 work items (rows * num_kv_heads * ceil(topk / 512)). */

@@ -104,7 +104,8 @@ int check_decode_args(const qsa_b200_decode_args* a) {
     if (a->num_pages * a->page_size * a->num_kv_heads > 0x7fffffffll) return QSA_B200_ERR_UNSUPPORTED;
     const int64_t chunk = tc_chunk_tokens(group);
     const int64_t chunks = a->topk <= chunk ? 1 : (a->topk + chunk - 1) / chunk;
-    if ((int64_t)a->rows * a->num_kv_heads * chunks > 0x3fffffffll) return QSA_B200_ERR_UNSUPPORTED;
+    const int64_t heads = (int64_t)a->num_kv_heads * (group > kMaxGroupTc ? 2 : 1);  // items count virtual heads
+    if ((int64_t)a->rows * heads * chunks > 0x3fffffffll) return QSA_B200_ERR_UNSUPPORTED;
   }
   if (a->rows == 0) return QSA_B200_OK;
   if (!a->q || !a->k_cache || !a->v_cache || !a->gate || !a->out) return QSA_B200_ERR_NULL_POINTER;

@@ -658,12 +658,14 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
           return false;
         }
         const int4 t = *reinterpret_cast<const int4*>(tab + j * kTile + lane * 4);
-        const int hkv = p.num_kv_heads;
+        // the cache's own KV heads (items count the virtual ones of a split group)
+        const int hkv = p.num_kv_heads >> p.kv_shift;
+        const int gk = g >> p.kv_shift;
         if (lane == 0) mbar_arrive_expect_tx(kv_full + s, kTileBytes);
         __syncwarp();
         tma_gather4(base_s + C::kSlotBase + (uint32_t)s * kTileBytes + (uint32_t)lane * 512u, map, kv_full + s,
-                    t.x >= 0 ? t.x * hkv + g : -1, t.y >= 0 ? t.y * hkv + g : -1, t.z >= 0 ? t.z * hkv + g : -1,
-                    t.w >= 0 ? t.w * hkv + g : -1);
+                    t.x >= 0 ? t.x * hkv + gk : -1, t.y >= 0 ? t.y * hkv + gk : -1,
+                    t.z >= 0 ? t.z * hkv + gk : -1, t.w >= 0 ? t.w * hkv + gk : -1);
       }
       return true;
     };
@@ -1230,10 +1232,10 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   const int64_t items = (int64_t)p.rows * p.num_kv_heads * p.num_chunks;
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
-  if (p.num_pages * p.page_size * p.num_kv_heads > 0x7fffffffll) return cudaErrorInvalidValue;
+  const int64_t rows = p.num_pages * p.page_size * (p.num_kv_heads >> p.kv_shift);  // of the caches
+  if (rows > 0x7fffffffll) return cudaErrorInvalidValue;
   if (!p.rowmap || !p.tile_flags || !p.item_counter || p.rowmap_stride != p.num_chunks * C::kChunk)
     return cudaErrorInvalidValue;
-  const int64_t rows = p.num_pages * p.page_size * p.num_kv_heads;
   CUtensorMap mk, mv;
   if (!encode_rows(&mk, p.k, rows) || !encode_rows(&mv, p.v, rows)) return cudaErrorInvalidValue;
   const int grid = (int)(items < sm_count() ? items : sm_count());
@@ -1263,7 +1265,7 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
 int tc_chunk_tokens(int) { return 4 * kTile; }
 
 bool tc_supports_group(int group) {
-  return group >= 1 && group <= kMaxGroupTc;
+  return (group >= 1 && group <= kMaxGroupTc) || (group <= 2 * kMaxGroupTc && group % 2 == 0);
 }
 
 // Split rows merge in the CTA when there are enough (row, KV head) pairs to
@@ -1279,7 +1281,20 @@ bool tc_merges_chunks(const DecodeParams& p) {
 
 cudaError_t launch_decode_tc(const DecodeParams& params, cudaStream_t stream) {
   DecodeParams p = params;
-  p.merge_chunks = tc_merges_chunks(params) ? 1 : 0;
+  p.kv_shift = 0;
+  if (p.group > kMaxGroupTc) {
+    // an even group of 18 .. 32 query heads runs as two virtual KV heads of
+    // half the group each: virtual head gv reads cache head gv >> 1, and its
+    // query heads gv * G/2 .. are exactly the second or first half of the
+    // real group's (the q, gate and out layouts need no change); the two
+    // items of a KV head run on neighbouring CTAs, so the second read of a
+    // row mostly finds it in L2
+    if (p.group % 2 != 0 || p.group > 2 * kMaxGroupTc) return cudaErrorInvalidValue;
+    p.group /= 2;
+    p.num_kv_heads *= 2;
+    p.kv_shift = 1;
+  }
+  p.merge_chunks = tc_merges_chunks(p) ? 1 : 0;
   switch (p.group) {
     case 1: return launch_g<1>(p, stream);
     case 2: return launch_g<2>(p, stream);

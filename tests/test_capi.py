@@ -83,7 +83,7 @@ def _args_cpu(**over):
     (dict(indices_stride=10), -2),
     (dict(btable_stride=2), -2),
     (dict(kernel=7), -3),
-    (dict(num_q_heads=8 * 17, kernel=1), -3),  # G = 17: above 16 runs on the CUDA-core kernel only
+    (dict(num_q_heads=8 * 17, kernel=1), -3),  # G = 17: odd above 16 runs on the CUDA-core kernel only
     # tensor-core kernel limits: 2^24 pages x 16 x 8 KV heads = 2^31 rows of
     # 128 bytes; 2^24 rows x 8 KV heads x 8 chunks = 2^30 work items
     (dict(num_pages=1 << 24), -3),
@@ -138,7 +138,7 @@ def test_workspace_sizes():
     rowmap = 4 * 3 * 512 * 4 + 256 + 256
     assert capi.workspace_bytes(a) == rowmap + n * 512 + n * 4 == ops.workspace_bytes(4, 32, 8, 1100)
     a256 = lambda x: -(-x // 256) * 256
-    for hq in (128, 96, 72):  # groups 16, 12, 9: tensor-core kernel, 512-entry chunks like every group
+    for hq in (128, 96, 72, 256):  # groups 16, 12, 9, 32: tensor-core kernel, 512-entry chunks like every group
         a.num_q_heads = hq
         n = 4 * hq * 3
         assert capi.workspace_bytes(a) == rowmap + n * 512 + a256(n * 4) == ops.workspace_bytes(4, hq, 8, 1100)
