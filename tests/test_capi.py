@@ -192,3 +192,18 @@ def test_merge_policy_mirror():
     assert not ops.tc_merges_chunks(1024, 64, 8, 512, 148)
     assert not ops.tc_merges_chunks(1024, 64, 8, 512 * 33, 148)
     assert ops.tc_merges_chunks(37, 32, 8, 1600, 148) and not ops.tc_merges_chunks(36, 32, 8, 1600, 148)
+
+
+def test_group_support_mirror_matches_the_library():
+    """ops.tc_supports_group (used to size workspaces on the Python side)
+    agrees with the library for every group size: the tensor-core kernel
+    takes 1 to 16 and the even sizes up to 32, and refuses the others."""
+    from qsa_b200 import capi, ops
+
+    for g in range(1, 34):
+        a = _args_cpu(num_q_heads=8 * g, kernel=capi.KERNEL_TC)
+        a.indices = a.btable = a.q = a.k_cache = a.v_cache = a.gate = a.out = ctypes.c_void_p(4096)
+        got = capi.workspace_bytes(a)
+        assert (got >= 0) == ops.tc_supports_group(g), (g, got)
+        if got < 0:
+            assert got == capi.ERR_UNSUPPORTED
