@@ -64,10 +64,10 @@ enum {
   QSA_B200_ERR_BAD_VALUE = -10    /* a scale is not a positive finite number */
 };
 
-/* Kernel selection. AUTO picks the tensor-core kernel for group sizes
- * (Hq / Hkv) 1 to 16 and the even ones up to 32 (each KV head's query heads
- * in two halves, each half reading the KV rows), and the CUDA-core kernel for
- * the odd ones from 17 to 31. The tensor-core kernel (explicit or through AUTO)
+/* Kernel selection. AUTO picks the tensor-core kernel for every group size
+ * (Hq / Hkv) from 1 to 32; above 16 each KV head's query heads go in two
+ * halves, each half reading the KV rows. The CUDA-core kernel (SIMT) takes
+ * the same sizes. The tensor-core kernel (explicit or through AUTO)
  * returns QSA_B200_ERR_UNSUPPORTED for a cache of more than 2^31 - 1 rows of
  * 128 bytes (num_pages * page_size * num_kv_heads; 256 GiB per cache) and
  * for more than 2^30 - 1 work items (rows * num_kv_heads * ceil(topk / 512)). */

@@ -205,6 +205,24 @@ __device__ __forceinline__ Item item_of(const DecodeParams& p, int item) {
   return it;
 }
 
+// Query heads of (virtual) KV head g: they start at q_head0 and there are
+// q_heads of them. Without kMap, head g's are g * G .. g * G + G - 1 (also for
+// an even group above 16 split into two virtual heads of G each). With kMap
+// (an odd group above 16, split into virtual heads of G and G - 1 query
+// heads), the first half of cache head g >> 1 holds G of its real_group
+// heads and the second half the rest plus a padding head: zero query rows,
+// never stored. The kernel instances without kMap carry none of this.
+template <int G, bool kMap>
+__device__ __forceinline__ int q_head0(const DecodeParams& p, int g) {
+  if constexpr (kMap) return (g >> 1) * p.real_group + (g & 1) * G;
+  return g * G;
+}
+template <int G, bool kMap>
+__device__ __forceinline__ int q_heads(const DecodeParams& p, int g) {
+  if constexpr (kMap) return (g & 1) ? p.real_group - G : G;
+  return G;
+}
+
 // The decoder's walk over the items when rows are split (num_chunks > 1).
 // Items are taken in windows of w claim indices. Claim index c stands for
 // (row, chunk) rc = c % (rows * num_chunks) and KV head c / (rows *
@@ -258,7 +276,7 @@ __device__ __forceinline__ void walk_init(ItemWalk& wk, const DecodeParams& p, i
 }
 
 // The next item of the walk (with kLastChunk where it applies), -1 at its end.
-template <int G>
+template <int G, bool kMap>
 __device__ __forceinline__ int walk_next(ItemWalk& wk, const DecodeParams& p, int num_items, int lane) {
   while (wk.live == 0u) {
     if (wk.next_base >= num_items) return -1;
@@ -272,16 +290,17 @@ __device__ __forceinline__ int walk_next(ItemWalk& wk, const DecodeParams& p, in
       if (in && !keep) {
         const Item w = item_of(p, claim_item(p, c));
 #pragma unroll 1
-        for (int h = 0; h < G; ++h)
-          p.part_lse[((int64_t)w.row * p.num_q_heads + w.g * G + h) * p.num_chunks + w.chunk] = -INFINITY;
+        for (int h = 0; h < q_heads<G, kMap>(p, w.g); ++h)
+          p.part_lse[((int64_t)w.row * p.num_q_heads + q_head0<G, kMap>(p, w.g) + h) * p.num_chunks + w.chunk] =
+              -INFINITY;
       }
     } else if (wk.live == 0u) {
       // a (row, KV head) without a valid entry: its G heads are zeros
       const Item w = item_of(p, claim_item(p, wk.base));
 #pragma unroll 1
-      for (int h = 0; h < G; ++h)
-        *reinterpret_cast<uint2*>(p.out + ((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim + lane * 4) =
-            make_uint2(0u, 0u);
+      for (int h = 0; h < q_heads<G, kMap>(p, w.g); ++h)
+        *reinterpret_cast<uint2*>(p.out + ((int64_t)w.row * p.num_q_heads + q_head0<G, kMap>(p, w.g) + h) * kHeadDim +
+                                  lane * 4) = make_uint2(0u, 0u);
     }
     // the window after it (claimed one window ago) and a claim for the one after that
     wk.next_base = __shfl_sync(0xffffffffu, wk.claim, 0);
@@ -440,7 +459,7 @@ __device__ __forceinline__ float combine_p(const float* v) {
 
 // kSplit: rows are split into several chunks (num_chunks > 1). A separate
 // instance keeps the unsplit loop free of the walk's code.
-template <int G, bool kSplit>
+template <int G, bool kSplit, bool kMap>
 __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     qsa_decode_tc_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
                          const __grid_constant__ CUtensorMap tmap_v, int num_items) {
@@ -524,10 +543,12 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     auto load_q = [&](int item, uint2 (&q)[G]) {
       if ((item & kItemMask) < num_items) {
         const Item w = item_of(p, item);
+        const int h0 = q_head0<G, kMap>(p, w.g), nh = q_heads<G, kMap>(p, w.g);
 #pragma unroll
         for (int h = 0; h < G; ++h)
-          q[h] = *reinterpret_cast<const uint2*>(p.q + ((int64_t)w.row * p.num_q_heads + w.g * G + h) * kHeadDim +
-                                                 lane * 4);
+          q[h] = h < nh ? *reinterpret_cast<const uint2*>(p.q + ((int64_t)w.row * p.num_q_heads + h0 + h) * kHeadDim +
+                                                          lane * 4)
+                        : make_uint2(0u, 0u);  // a split odd group's padding head
       }
     };
     uint2 q_n[G];
@@ -541,7 +562,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
     int nx = 0;
     if (split) {
       walk_init(wk, p, num_items, lane);
-      nx = walk_next<G>(wk, p, num_items, lane);
+      nx = walk_next<G, kMap>(wk, p, num_items, lane);
       if (nx >= 0 && (nx & kItemMask) != item_at(0)) load_q(nx, q_n);
     }
     int k = 0;  // published items so far
@@ -553,7 +574,7 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
 #pragma unroll
       for (int h = 0; h < G; ++h) q_c[h] = q_n[h];
       if (!last) {
-        nx = split ? walk_next<G>(wk, p, num_items, lane) : (nx + 1 < n_my ? nx + 1 : -1);
+        nx = split ? walk_next<G, kMap>(wk, p, num_items, lane) : (nx + 1 < n_my ? nx + 1 : -1);
         if (nx >= 0) load_q(split ? nx : item_at(nx), q_n);
       }
 
@@ -858,8 +879,8 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
         const float o = (e_any && e_l[hh] > 0.f)
                             ? __fdividef(combine_p(v + hh * kTermsP) * (1.0f / 256.0f), e_l[hh])
                             : 0.f;
-        if (h >= G) continue;  // the padding head of an odd group
-        const int64_t hrow = (int64_t)e_row * p.num_q_heads + e_g * G + h;
+        if (h >= q_heads<G, kMap>(p, e_g)) continue;  // a padding head (odd group, or a split odd group's half)
+        const int64_t hrow = (int64_t)e_row * p.num_q_heads + q_head0<G, kMap>(p, e_g) + h;
         if (p.num_chunks == 1) {
           const float gt = __bfloat162float(e_gate[hh]);
           // exp(80) keeps 1 + e below 2^126, where the fast division is exact enough
@@ -923,8 +944,9 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 1)
       if (split ? p.merge_chunks != 0 : p.num_chunks == 1) {
 #pragma unroll
         for (int hh = 0; hh < C::kHalfHeads; ++hh)
-          gate[hh] = h0 + hh < G ? p.gate[((int64_t)w.row * p.num_q_heads + w.g * G + h0 + hh) * kHeadDim + tk]
-                                 : __float2bfloat16_rn(0.f);
+          gate[hh] = h0 + hh < q_heads<G, kMap>(p, w.g)
+                         ? p.gate[((int64_t)w.row * p.num_q_heads + q_head0<G, kMap>(p, w.g) + h0 + hh) * kHeadDim + tk]
+                         : __float2bfloat16_rn(0.f);
       }
       // meta_full publishes the row table and query scales; s_full the
       // scores. Once anything failed the group keeps walking its items (the
@@ -1205,7 +1227,7 @@ int sm_count() {
   return c;
 }
 
-template <int G>
+template <int G, bool kMap = false>
 cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   using C = Cfg<G>;
   static std::atomic<uint64_t> configured{0};
@@ -1214,10 +1236,10 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(qsa_decode_tc_kernel<G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(qsa_decode_tc_kernel<G, false, kMap>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmemAlloc);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(qsa_decode_tc_kernel<G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(qsa_decode_tc_kernel<G, true, kMap>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmemAlloc);
     if (e != cudaSuccess) return e;
     // the row-map kernel asks for the decode's shared-memory carveout, so
@@ -1256,8 +1278,8 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return p.num_chunks > 1 ? cudaLaunchKernelEx(&cfg, qsa_decode_tc_kernel<G, true>, p, mk, mv, (int)items)
-                          : cudaLaunchKernelEx(&cfg, qsa_decode_tc_kernel<G, false>, p, mk, mv, (int)items);
+  return p.num_chunks > 1 ? cudaLaunchKernelEx(&cfg, qsa_decode_tc_kernel<G, true, kMap>, p, mk, mv, (int)items)
+                          : cudaLaunchKernelEx(&cfg, qsa_decode_tc_kernel<G, false, kMap>, p, mk, mv, (int)items);
 }
 
 }  // namespace
@@ -1265,7 +1287,7 @@ cudaError_t launch_g(const DecodeParams& p, cudaStream_t stream) {
 int tc_chunk_tokens(int) { return 4 * kTile; }
 
 bool tc_supports_group(int group) {
-  return (group >= 1 && group <= kMaxGroupTc) || (group <= 2 * kMaxGroupTc && group % 2 == 0);
+  return group >= 1 && group <= 2 * kMaxGroupTc;
 }
 
 // Split rows merge in the CTA when there are enough (row, KV head) pairs to
@@ -1282,19 +1304,32 @@ bool tc_merges_chunks(const DecodeParams& p) {
 cudaError_t launch_decode_tc(const DecodeParams& params, cudaStream_t stream) {
   DecodeParams p = params;
   p.kv_shift = 0;
+  p.real_group = p.group;
   if (p.group > kMaxGroupTc) {
-    // an even group of 18 .. 32 query heads runs as two virtual KV heads of
-    // half the group each: virtual head gv reads cache head gv >> 1, and its
-    // query heads gv * G/2 .. are exactly the second or first half of the
-    // real group's (the q, gate and out layouts need no change); the two
-    // items of a KV head run on neighbouring CTAs, so the second read of a
-    // row mostly finds it in L2
-    if (p.group % 2 != 0 || p.group > 2 * kMaxGroupTc) return cudaErrorInvalidValue;
-    p.group /= 2;
+    // a group of 17 .. 32 query heads runs as two virtual KV heads, the
+    // first with ceil(G / 2) of the query heads and the second with the
+    // rest (for an odd G one less, plus a padding head): virtual head gv
+    // reads cache head gv >> 1, and q_head0 / q_heads map it to its query
+    // heads; the two items of a KV head run on neighbouring CTAs
+    if (p.group > 2 * kMaxGroupTc) return cudaErrorInvalidValue;
+    p.group = (p.group + 1) / 2;
     p.num_kv_heads *= 2;
     p.kv_shift = 1;
   }
   p.merge_chunks = tc_merges_chunks(p) ? 1 : 0;
+  if (p.kv_shift && p.real_group % 2 != 0) {  // an odd group above 16: the explicit head map
+    switch (p.group) {
+      case 9: return launch_g<9, true>(p, stream);
+      case 10: return launch_g<10, true>(p, stream);
+      case 11: return launch_g<11, true>(p, stream);
+      case 12: return launch_g<12, true>(p, stream);
+      case 13: return launch_g<13, true>(p, stream);
+      case 14: return launch_g<14, true>(p, stream);
+      case 15: return launch_g<15, true>(p, stream);
+      case 16: return launch_g<16, true>(p, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (p.group) {
     case 1: return launch_g<1>(p, stream);
     case 2: return launch_g<2>(p, stream);

@@ -65,8 +65,10 @@ struct DecodeParams {
   // kernel); set by the launcher from tc_merges_chunks.
   int merge_chunks;
   // Tensor-core kernel: log2 of the virtual KV heads per cache KV head (1
-  // when a group above 16 runs as two halves); set by the launcher.
+  // when a group above 16 runs as two halves), and the caches' own group
+  // size Hq / Hkv; set by the launcher.
   int kv_shift;
+  int real_group;
 
   int* err;  // device error word of the current device
   // Limit of each pipeline wait of the tensor-core kernel, in ns of

@@ -187,10 +187,9 @@ def token_slots(btable, reqs, positions, page_size):
 
 
 def tc_supports_group(group: int) -> bool:
-    """Group sizes (Hq / Hkv) of the tensor-core kernel: 1 to 16, and the even
-    sizes up to 32 (run as two halves per KV head); odd ones above 16 run on
-    the CUDA-core kernel."""
-    return 1 <= group <= 16 or (group <= 32 and group % 2 == 0)
+    """Group sizes (Hq / Hkv) of the tensor-core kernel: 1 to 32 (above 16 as
+    two halves per KV head), every size the library takes."""
+    return 1 <= group <= 32
 
 
 def tc_merges_chunks(rows: int, num_q_heads: int, num_kv_heads: int, topk: int, sm_count: int) -> bool:

@@ -83,7 +83,6 @@ def _args_cpu(**over):
     (dict(indices_stride=10), -2),
     (dict(btable_stride=2), -2),
     (dict(kernel=7), -3),
-    (dict(num_q_heads=8 * 17, kernel=1), -3),  # G = 17: odd above 16 runs on the CUDA-core kernel only
     # tensor-core kernel limits: 2^24 pages x 16 x 8 KV heads = 2^31 rows of
     # 128 bytes; 2^24 rows x 8 KV heads x 8 chunks = 2^30 work items
     (dict(num_pages=1 << 24), -3),
@@ -138,13 +137,14 @@ def test_workspace_sizes():
     rowmap = 4 * 3 * 512 * 4 + 256 + 256
     assert capi.workspace_bytes(a) == rowmap + n * 512 + n * 4 == ops.workspace_bytes(4, 32, 8, 1100)
     a256 = lambda x: -(-x // 256) * 256
-    for hq in (128, 96, 72, 256):  # groups 16, 12, 9, 32: tensor-core kernel, 512-entry chunks like every group
+    for hq in (128, 96, 72, 256, 136):  # groups 16, 12, 9, 32, 17: tensor-core kernel, 512-entry chunks
         a.num_q_heads = hq
         n = 4 * hq * 3
         assert capi.workspace_bytes(a) == rowmap + n * 512 + a256(n * 4) == ops.workspace_bytes(4, hq, 8, 1100)
-    a.num_q_heads = 136  # group 17: CUDA-core kernel, no row map
+    a.num_q_heads, a.kernel = 136, capi.KERNEL_SIMT  # the CUDA-core kernel: no row map
     n = 4 * 136 * 3
-    assert capi.workspace_bytes(a) == n * 512 + a256(n * 4) == ops.workspace_bytes(4, 136, 8, 1100)
+    assert capi.workspace_bytes(a) == n * 512 + a256(n * 4) == ops.workspace_bytes(4, 136, 8, 1100, kernel="simt")
+    a.kernel = capi.KERNEL_AUTO
     # enough (row, KV head) pairs for the decode kernel to merge the chunks
     # itself (at least two per SM): no partials
     a.num_q_heads, a.rows, a.num_reqs = 32, 1024, 1024
@@ -197,7 +197,7 @@ def test_merge_policy_mirror():
 def test_group_support_mirror_matches_the_library():
     """ops.tc_supports_group (used to size workspaces on the Python side)
     agrees with the library for every group size: the tensor-core kernel
-    takes 1 to 16 and the even sizes up to 32, and refuses the others."""
+    takes 1 to 32 and refuses the others."""
     from qsa_b200 import capi, ops
 
     for g in range(1, 34):

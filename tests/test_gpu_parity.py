@@ -204,6 +204,7 @@ def test_ragged_gqa8_split(kernel):
     (80, 8, "tc"), (96, 8, "tc"), (112, 8, "tc"),
     (72, 8, "tc"), (88, 8, "tc"), (104, 8, "tc"), (120, 8, "tc"),
     (144, 8, "tc"), (256, 8, "tc"), (32, 1, "tc"), (20, 1, "tc"), (136, 8, "auto"),
+    (136, 8, "tc"), (152, 8, "tc"), (248, 8, "tc"), (17, 1, "tc"), (31, 1, "tc"),
     (24, 8, "simt"), (48, 8, "simt"), (32, 8, "simt"), (32, 4, "tc"), (32, 1, "simt"), (72, 8, "auto"),
 ])
 def test_group_sizes(hq, hkv, kernel):
@@ -218,7 +219,8 @@ def test_group_sizes(hq, hkv, kernel):
     assert max_ulps(bits(out), ref) <= 1.0
 
 
-@pytest.mark.parametrize("hq,hkv", [(24, 8), (56, 8), (72, 8), (96, 8), (112, 8), (120, 8), (256, 8), (32, 1)])
+@pytest.mark.parametrize("hq,hkv", [(24, 8), (56, 8), (72, 8), (96, 8), (112, 8), (120, 8), (256, 8), (32, 1),
+                                     (136, 8), (31, 1)])
 def test_group_sizes_split(hq, hkv):
     """Odd and padded group sizes on the tensor-core kernel with a Top-K long
     enough to split into chunks (512 entries per chunk up to G = 8, 256
