@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--config 1|2|3|4] [--kernel auto|tc|simt] [--op decode|cache_write|topk]
+                    [--rows R]
 
 Workload (``--config``), one process per GPU under torchrun, requests sharded
 by rank with no data-path collective:
@@ -112,7 +113,13 @@ def parse():
     ap.add_argument("--op", choices=["decode", "cache_write", "topk"], default="decode")
     ap.add_argument("--no-per-config", action="store_true", help="skip the configs[2]/[4] block at N=1")
     ap.add_argument("--check-rows", type=int, default=8, help="rows per rank checked after the timed steps")
-    return ap.parse_args()
+    ap.add_argument("--rows", type=int, default=None,
+                    help="configs 1 and 2: requests per GPU of the configuration's shape (default: its own count); "
+                         "for smaller profiling captures")
+    a = ap.parse_args()
+    if a.rows is not None and (a.rows < 1 or SCALING.get(a.config) != "weak"):
+        ap.error("--rows takes a positive count and applies to configs 1 and 2 only")
+    return a
 
 
 def peaks():
@@ -292,12 +299,13 @@ def reduce_sum(x: float, world: int, local: int) -> float:
 SCALING = {0: "weak", 1: "weak", 2: "weak", 3: "strong", 4: "strong"}
 
 
-def rank_rows(cfg: int, rank: int, world: int):
+def rank_rows(cfg: int, rank: int, world: int, rows: int | None = None):
     """Which requests of the configuration rank ``rank`` of ``world`` holds:
     ``(rows, row_ids, plan)`` -- a row count (weak scaling: the whole
-    configuration per rank) or the row ids of its shard (configs[3]:
-    contiguous ranges of the 2048 requests; configs[4]: longest-processing-
-    time bins over the 1024 ragged Top-K lengths)."""
+    configuration per rank, or ``rows`` of its shape when given) or the row
+    ids of its shard (configs[3]: contiguous ranges of the 2048 requests;
+    longest-processing-time bins over the 1024 ragged Top-K
+    lengths)."""
     from qsa_b200.inputs import CONFIGS, ragged_lengths
     from qsa_b200.shard import bin_loads, contiguous_shards, lpt_bins
 
@@ -311,13 +319,15 @@ def rank_rows(cfg: int, rank: int, world: int):
         loads = bin_loads(lengths, bins)
         return None, bins[rank], (f"LPT bin {rank} of {world}: {len(bins[rank])} of {total} rows, "
                                   f"{loads[rank]} of {sum(loads)} Top-K entries (bins {min(loads)}-{max(loads)})")
+    if rows:
+        return rows, None, f"{rows} rows of the configuration's shape on every rank"
     return total, None, f"all {total} rows of the configuration on every rank"
 
 
-def make_rank_workload(cfg: int, dev, rank: int, world: int):
+def make_rank_workload(cfg: int, dev, rank: int, world: int, rows: int | None = None):
     from qsa_b200.inputs import make_workload
 
-    rows, row_ids, plan = rank_rows(cfg, rank, world)
+    rows, row_ids, plan = rank_rows(cfg, rank, world, rows)
     w = make_workload(cfg, dev, seed=0, rows=rows, row_ids=row_ids, shard=rank)
     return w, plan
 
@@ -332,11 +342,11 @@ def bench_config(cfg: int, world: int, rows_per_gpu: int, rows_total: int) -> di
             "topk": c["topk"], "parallelism": f"request-sharded x{world}, no collective"}
 
 
-def config_rows(cfg: int, world: int):
+def config_rows(cfg: int, world: int, rows: int | None = None):
     """(rows per GPU, rows in the job): the largest shard for strong scaling."""
     from qsa_b200.inputs import CONFIGS
 
-    total = CONFIGS[cfg]["rows"]
+    total = (rows or CONFIGS[cfg]["rows"]) if SCALING[cfg] == "weak" else CONFIGS[cfg]["rows"]
     if SCALING[cfg] == "weak":
         return total, total * world
     return max(len(rank_rows(cfg, r, world)[1]) for r in range(world)), total
@@ -430,8 +440,8 @@ def run_reference_arm(args):
     from qsa_b200.inputs import make_workload
 
     cfg = args.config
-    rows_gpu, rows_total = config_rows(cfg, args.gpus)
-    _, row_ids, _ = rank_rows(cfg, 0, args.gpus)
+    rows_gpu, rows_total = config_rows(cfg, args.gpus, args.rows)
+    _, row_ids, _ = rank_rows(cfg, 0, args.gpus, args.rows)
 
     def sample_workload(n):
         if row_ids is not None:
@@ -748,7 +758,7 @@ def run_ours(args):
     import qsa_b200
 
     cfg = args.config
-    w, plan = make_rank_workload(cfg, dev, rank, world)
+    w, plan = make_rank_workload(cfg, dev, rank, world, args.rows)
     acct = kv_bytes(w)
     flush = L2Flush(dev)
     out = torch.empty_like(w.q)
@@ -849,8 +859,9 @@ def run_ours(args):
 
     achieved_gbs = acct["algorithmic"] / (local_ms * 1e-3) / 1e9
     kname = "tc" if kernel in ("auto", "tc") else kernel
-    traffic, traffic_source = NCU_TRAFFIC.get((workload_name(cfg), kname), (None, None))
-    rows_gpu, rows_total = config_rows(cfg, world)
+    traffic, traffic_source = (NCU_TRAFFIC.get((workload_name(cfg), kname), (None, None)) if not args.rows
+                               else (None, None))
+    rows_gpu, rows_total = config_rows(cfg, world, args.rows)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
