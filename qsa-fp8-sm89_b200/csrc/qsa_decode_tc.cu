@@ -13,6 +13,8 @@
 // its own.
 //
 // Work item = (Top-K row, KV head, chunk of up to kTiles*128 Top-K entries).
+// A group of more than 16 query heads runs as two virtual KV heads per cache
+// KV head, each with about half of the query heads (launch_decode_tc).
 // With unsplit rows each CTA (one per SM) takes items blockIdx.x,
 // blockIdx.x + gridDim.x, ... (its k-th item is blockIdx.x + k * gridDim.x,
 // k < n_my). With split rows it walks windows of items claimed from a
