@@ -17,11 +17,13 @@ from gpu_helpers import bits, check_close
 from oracle import qsa_oracle as O
 
 # (workload config, overrides, rows): split-K with G 4 (3 chunks of 512),
-# ragged G 8 with per-row counts (4 chunks), and a single-chunk shape that
-# uses no scratch at all
+# ragged G 8 with per-row counts (4 chunks), split-K with G 17 (two virtual
+# KV heads per cache head, partials for every query head), and a
+# single-chunk shape that uses no scratch at all
 SHAPES = {
     "split_g4": (0, dict(ppr=100, topk=1500, mode="sample"), 64),
     "ragged_g8": (4, dict(ppr=160, topk=2048, len_lo=64, len_hi=2048), 32),
+    "split_g17": (0, dict(hq=136, hkv=8, ppr=100, topk=1500, mode="sample"), 16),
     "one_chunk": (1, {}, 32),
 }
 
